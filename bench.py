@@ -1,0 +1,377 @@
+"""Benchmark: one QSA layer decode step (indexer -> top-k -> sparse attention).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2_32k] [--impl ours|reference]
+
+Workload (``--config``, default the headline ``cfg2_32k``): batch 64 decode
+rows at 32768 tokens of context, 32 query / 4 KV heads of dim 128 (bf16),
+indexer 8 heads x 64 with U(0,1) head weights, compress ratio 4, top-k 2048
+tokens (512 blocks), page 64, seeded random block tables.  A step is the whole
+QSA path of one layer for those 64 rows, run as vLLM runs decode: through the
+drop-in operators (``select_paged_tokens`` + ``qsa_sparse_paged_attention``)
+captured in a CUDA graph.  Inputs are synthetic (seeded N(0,1) / U(0,1)).
+
+Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on
+the launching stream, with the L2 flushed (256 MiB write) before every step
+outside the events; max over ranks.  With ``--gpus N`` (torchrun, NCCL) the
+heads are sharded across ranks as vLLM tensor parallelism does (no
+collective inside the path; the indexer is replicated), so the total work is
+fixed: ``value`` = rows / (max-over-ranks step time).
+
+``e2e`` re-times the same step through the public Python API eagerly with the
+step's inputs copied host->device from pinned memory and the attention output
+copied back, inside the timed region.  ``roofline`` times the dominant kernel
+(sparse attention) alone.  ``cpu_baseline`` times the CPU oracle on a bounded
+sample of rows on this host.  ``--impl reference`` runs the reference math
+(the CPU oracle port, the only form of the reference's path that runs without
+its vLLM 0.30 / SM80 stack) with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "QSA decode tokens/s/GPU @32k ctx, top-k 2048; % HBM and tensor-pipe roofline"
+UNIT = "tokens/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def workload_desc(cfg: str, w) -> dict:
+    c = w.extra["config"]
+    return {
+        "workload": (f"{cfg}: one QSA layer decode step (indexer + top-k + sparse attention), "
+                     f"B={w.rows}, ctx {c['seq_len']}, H_q {c['hq']} / H_kv {c['hkv']} x d "
+                     f"{c['d']} bf16, indexer {c['hi']}x{c['di']} (U(0,1) head weights), "
+                     f"ratio {w.ratio}, top-k {w.token_topk} tokens, page {w.page_size}"),
+        "global_batch": w.rows,
+        "seq_len": c["seq_len"] if not isinstance(c["seq_len"], tuple) else list(c["seq_len"]),
+        "l2": "flushed before every timed step (256 MiB write, outside the events)",
+        "cuda_graph": True,
+    }
+
+
+def algorithmic_bytes(w) -> dict:
+    """Bytes each stage must move at least once (no credit for cache reuse).
+
+    attention: every selected token's K and V row of every KV head (2*d bf16
+    each), its index, plus q, gate and out; indexer: every visible compressed
+    key (d_i bf16) + the fp32 score written; top-k: scores read + ids written.
+    """
+    rows, hq, d = w.q.shape
+    hkv = w.kv.shape[2]
+    r = w.ratio
+    k_blk = w.token_topk // r
+    width = w.token_topk + r - 1
+    pos1 = w.positions.long().cpu() + 1
+    seq = w.seq_lens.long().cpu()[w.token_to_req.long().cpu()]
+    vis = torch.minimum(pos1 // r, seq // r)
+    complete = torch.clamp(vis, max=k_blk)
+    count = torch.minimum(complete * r + (pos1 - (pos1 // r) * r), seq)
+    sel = int(count.sum())
+    vis_total = int(vis.sum())
+    hi, di = w.index_q.shape[1], w.index_q.shape[2]
+    att = sel * hkv * 2 * d * 2 + sel * 4 + 3 * rows * hq * d * 2
+    idx = vis_total * di * 2 + rows * hi * di * 2 + vis_total * 4
+    topk = vis_total * 4 + rows * width * 4
+    return {"attention": att, "indexer": idx, "topk": topk, "rows": rows,
+            "attention_flops": sel * hq * d * 4, "indexer_flops": vis_total * hi * di * 2}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.proc is None or not self.path:
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(cfg: str, rows: int = 4, min_seconds: float = 10.0) -> dict:
+    """The CPU oracle on a bounded sample: ``rows`` rows of the same workload."""
+    from oracle import qsa_oracle as O
+    from qsa_vllm_b200.synthetic import make_workload
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = make_workload(cfg, device="cpu", seed=0, batch=rows)
+    O.decode_step(w)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.decode_step(w)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or n >= 50:
+            break
+    return {"value": rows * n / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rows} of the workload's rows ({cfg} per-row shapes) x {n} passes "
+                      f"of oracle.decode_step, {el:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import qsa_oracle as O
+    from qsa_vllm_b200.synthetic import make_workload
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = args.ref_rows
+    w = make_workload(args.config, device="cpu", seed=0, batch=rows)
+    for _ in range(args.warmup):
+        O.decode_step(w)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.decode_step(w)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = rows * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"{args.config} per-row shapes, {rows} rows per step "
+                               "(bounded CPU sample)", "global_batch": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows per step of {args.config} through the CPU "
+                                   "oracle (reference math restated in PyTorch eager)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2_32k")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-rows", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from qsa_vllm_b200.indexer import select_paged_tokens
+    from qsa_vllm_b200.qsa import attention_workspace_bytes, qsa_sparse_paged_attention
+    from qsa_vllm_b200.synthetic import make_workload
+
+    full = make_workload(args.config, device=dev, seed=args.seed)
+    w = full.shard_heads(world, rank) if world > 1 else full
+    del full
+    rows = w.rows
+    width = w.token_topk + w.ratio - 1
+    idx_buf = torch.empty(rows, width, dtype=torch.int32, device=dev)
+    cnt_buf = torch.empty(rows, dtype=torch.int32, device=dev)
+    out = torch.empty_like(w.q)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        select_paged_tokens(
+            w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
+            w.token_topk, w.ratio, idx_buf, query_start_loc=w.query_start_loc, max_query_len=1,
+            max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt_buf,
+            weights=w.index_weights, scale=w.index_scale)
+        qsa_sparse_paged_attention(w.q, w.k_cache, w.v_cache, idx_buf, w.block_table,
+                                   w.token_to_req, out, output_gate=w.gate,
+                                   use_decode_kernel=True, indices_are_physical=True,
+                                   valid_counts=cnt_buf)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+
+    def timed(fn, k):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(k)]
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in evs) / k   # ms per step
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed step (CUDA graph replay)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        ms = timed(graph.replay, args.steps)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms = max_over_ranks(ms)
+    value = rows / (ms * 1e-3)
+
+    # ---- dominant kernel alone: sparse attention (gather + split merge)
+    def attn():
+        qsa_sparse_paged_attention(w.q, w.k_cache, w.v_cache, idx_buf, w.block_table,
+                                   w.token_to_req, out, output_gate=w.gate,
+                                   use_decode_kernel=True, indices_are_physical=True,
+                                   valid_counts=cnt_buf)
+    attn()
+    ms_attn = max_over_ranks(timed(attn, args.steps))
+
+    # ---- end to end through the public API with host buffers
+    per_step = [w.q, w.gate, w.index_q, w.index_weights, w.positions, w.seq_lens,
+                w.token_to_req, w.block_table, w.index_table]
+    host_in = [t.cpu().pin_memory() for t in per_step]
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for dst, src in zip(per_step, host_in):
+            dst.copy_(src, non_blocking=True)
+        step()
+        host_out.copy_(out, non_blocking=True)
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms_e2e = max_over_ranks(timed(e2e_step, args.steps))
+    e2e_value = rows / (ms_e2e * 1e-3)
+
+    ab = algorithmic_bytes(w)
+    pk, pk_kind = peaks()
+    achieved = ab["attention"] / (ms_attn * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "attention_cfg2_32k_traffic.json"
+    if tf.exists() and world == 1 and args.config == "cfg2_32k":
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    need = attention_workspace_bytes(rows, w.q.shape[1], w.kv.shape[2], w.d, width, True)
+    launches_per_step = 3 + (1 if need else 0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config)
+    if dist is not None:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {**workload_desc(args.config, w),
+                   "parallelism": f"tp{world} head-sharded (indexer replicated)"},
+        "roofline": {
+            "kernel": "sparse attention (paged K/V gather + online softmax, + split merge)",
+            "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
+            "algorithmic_bytes_per_launch": ab["attention"], "ms_per_launch": ms_attn,
+            "traffic": traffic},
+        "stage_bytes": {k: ab[k] for k in ("attention", "indexer", "topk")},
+        "step_hbm_frac": (ab["attention"] + ab["indexer"] + ab["topk"]) / (ms * 1e-3) / 1e9
+        / pk["hbm_gbs"],
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+                "api": "select_paged_tokens + qsa_sparse_paged_attention, eager"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

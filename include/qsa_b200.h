@@ -1,0 +1,179 @@
+/*
+ * qsa_b200.h -- C ABI of the B200-native (sm_100a) QSA sparse-attention hot path.
+ *
+ * Three stages, one entry point each, plus plain helpers:
+ *   1. qsa_indexer_scores    dense q.k of every visible compressed index key,
+ *                            fused ReLU / head-weight / head-sum epilogue
+ *   2. qsa_topk_expand       exact per-row top-k of fp32 scores, expanded to
+ *                            token (or physical slot) ids plus the causal tail
+ *   3. qsa_sparse_attention  paged BF16 GQA attention over the selected tokens
+ *
+ * Conventions (every entry point):
+ *   - All pointers are device pointers of the current CUDA device, except
+ *     where a comment says otherwise.  bf16 tensors are passed as void*.
+ *   - Strides are in ELEMENTS of the pointed-to type, as torch reports them.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Nothing
+ *     synchronises the host; every launch is CUDA-graph capturable.
+ *   - No entry point allocates device memory.  Split-K attention takes a
+ *     caller-provided workspace sized by qsa_sparse_attention_workspace_bytes.
+ *   - Return value: QSA_OK or a QSA_ERR_* code; qsa_last_error() gives the
+ *     detail for the calling host thread.  Invalid metadata VALUES (a -1 page,
+ *     an out-of-range index) are not errors: they are masked exactly as the
+ *     reference masks them.
+ */
+#ifndef QSA_B200_H_
+#define QSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QSA_API __attribute__((visibility("default")))
+#else
+#define QSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qsa_status {
+  QSA_OK = 0,
+  QSA_ERR_INVALID = 1,     /* null pointer, negative size, misaligned / inconsistent strides */
+  QSA_ERR_UNSUPPORTED = 2, /* shape outside the compiled range (head dim, GQA group, width) */
+  QSA_ERR_WORKSPACE = 3,   /* workspace smaller than the matching *_workspace_bytes query */
+  QSA_ERR_CUDA = 4,        /* a CUDA runtime call or kernel launch failed */
+  QSA_ERR_DEVICE = 5,      /* the current device is not an sm_100 (B200) GPU */
+  QSA_ERR_TIMEOUT = 6      /* a bounded device-side wait expired (see qsa_device_error_poll) */
+};
+
+/* Human-readable name of a status code (static storage). */
+QSA_API const char* qsa_status_string(int status);
+/* Detail of the last failure on the calling host thread (thread-local storage). */
+QSA_API const char* qsa_last_error(void);
+/* Library version string. */
+QSA_API const char* qsa_version(void);
+/* QSA_OK when the current device is sm_100; QSA_ERR_DEVICE otherwise. */
+QSA_API int qsa_device_check(void);
+/*
+ * Reads and clears the device-side error word of the current device
+ * (synchronous: waits for the device).  0 = no error; otherwise a bit set of
+ * QSA_DEVICE_ERR_* recorded by kernels whose bounded waits expired.
+ */
+QSA_API int qsa_device_error_poll(int32_t* error_bits);
+enum { QSA_DEVICE_ERR_WAIT_TIMEOUT = 1 };
+
+/*
+ * Top-k selection + expansion.
+ * Replaces torch.ops.yulan_qsa_kernels.topk_expand
+ * (reference ops/csrc/topk.cu:503-525, schema :550-552; Python wrapper
+ * ops/topk.py:29-39; callers ops/indexer.py:273-279 and :336-343).
+ *
+ * For each row r: with L = min(lengths[r], score_width) and K = output_width / ratio,
+ * selects the K columns of scores[r, :L] with the largest fp32 BIT PATTERNS
+ * (uint32 order; ties to the lowest column), in ascending column order
+ * (all of 0..L-1 when L <= K), and expands selected block b to the tokens
+ * b*ratio .. b*ratio+ratio-1, followed by the causal tail of positions[r].
+ * physical != 0 maps tokens to slots page*page_size+offset through
+ * table[token_to_req[r]]; counts (nullable) receives the per-row valid count.
+ * scores: fp32 [rows, score_width] (unit column stride).
+ * positions: int64 [rows]; sequence_lengths: int32 [num_requests];
+ * token_to_req, lengths: int32 [rows]; output: int32 [rows, output_width].
+ */
+QSA_API int qsa_topk_expand(const float* scores, int64_t score_row_stride, int32_t rows,
+                    int32_t score_width, const int32_t* lengths, const int64_t* positions,
+                    const int32_t* sequence_lengths, int32_t num_requests,
+                    const int32_t* token_to_req, const int32_t* table,
+                    int64_t table_row_stride, int32_t table_width, int32_t* output,
+                    int64_t output_row_stride, int64_t output_col_stride,
+                    int32_t output_width, int32_t* counts, int32_t ratio, int32_t page_size,
+                    int32_t physical, void* stream);
+
+/*
+ * Plain top-k ids (no expansion).
+ * Replaces torch.ops.yulan_qsa_kernels.topk (reference ops/csrc/topk.cu:527-545,
+ * schema :549; wrapper ops/topk.py:25-26).  output: int32 [rows, topk], unit
+ * column stride; ids ascending, -1 padded when lengths[r] <= topk.
+ */
+QSA_API int qsa_topk(const float* scores, int64_t score_row_stride, int32_t rows, int32_t score_width,
+             const int32_t* lengths, int32_t* output, int64_t output_row_stride, int32_t topk,
+             void* stream);
+
+/*
+ * Indexer scores.
+ * Replaces the launches of _qsa_mqa_paged_uniform_kernel (reference
+ * ops/indexer.py:24-114, launched at :260-272) when query_start_loc == NULL,
+ * and of _qsa_mqa_paged_prefill_kernel (ops/indexer.py:117-223, launched by
+ * _prefill_logits :282-302) otherwise.
+ *
+ * logits[r - query_offset, c] = scale * sum_h w[r,h] * max(q[r,h,:] . key(c), 0)
+ * for packed rows r in [query_offset, query_offset + num_rows) and columns
+ * c < min(visible[r], table_width * page_size, logits_width); other logits are
+ * not written.  key(c) = k_cache[page_table[req(r), c / page_size], c % page_size].
+ * Decode (query_start_loc == NULL): req(r) = r / decode_query_len.
+ * Prefill: req(r) is the request whose [qsl[req]-qsl[0], qsl[req+1]-qsl[0])
+ * contains r; max_query_len bounds the rows of one request.
+ * q: bf16 [rows, num_heads, head_dim] (unit dim stride); k_cache: bf16
+ * [num_blocks, page_size, 1, head_dim] (unit dim stride); weights: fp32
+ * [rows, num_heads] or NULL for all ones (the reference's weighting);
+ * reference scale = head_dim ** -0.5.  head_dim must be 64 or 128.
+ */
+QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                       int32_t num_heads, int32_t head_dim, const void* k_cache,
+                       int64_t cache_block_stride, int64_t cache_token_stride,
+                       int32_t num_blocks, int32_t page_size, const int32_t* page_table,
+                       int64_t table_row_stride, int32_t table_width, int32_t num_requests,
+                       const int32_t* visible, const int32_t* query_start_loc,
+                       int32_t decode_query_len, int32_t max_query_len, int32_t query_offset,
+                       int32_t num_rows, const float* weights, int64_t weight_row_stride,
+                       int64_t weight_head_stride, float scale, float* logits,
+                       int64_t logits_row_stride, int32_t logits_width, void* stream);
+
+/*
+ * Workspace bytes qsa_sparse_attention needs for these shapes (0 when the
+ * launch plan uses a single split).  Deterministic in its arguments.
+ */
+QSA_API size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
+                                            int32_t num_kv_heads, int32_t head_dim,
+                                            int32_t topk_width, int32_t use_decode_kernel);
+
+/*
+ * Paged sparse GQA attention.
+ * Replaces qsa_sparse_paged_attention (reference ops/qsa.py:594-688):
+ * _qsa_sparse_paged_gqa_splitk_kernel (:109-303) and _qsa_merge_splitk_kernel
+ * (:306-362); called from YuLanQSAImpl.forward (backend.py:39-68).
+ *
+ * For row r and query head h (kv head h / (num_q_heads / num_kv_heads)):
+ *   out[r,h] = softmax_j(q[r,h] . K_j * head_dim^-0.5) . V_j over the columns j
+ *   of indices[r, :n] that resolve to a cached token, n = min(valid_counts[r],
+ *   topk_width) (topk_width when valid_counts is NULL).  P is rounded to bf16
+ *   before P.V; with a gate, out = bf16(out) * sigmoid(gate).  Rows with no
+ *   valid token get 0.
+ * indices_are_physical != 0: indices are slots page*page_size+offset.
+ * Otherwise indices are logical token ids of request token_to_req[r], mapped
+ * through block_table.  q, gate, out: bf16 [rows, num_q_heads, head_dim];
+ * k_cache / v_cache: bf16 [num_blocks, page_size, num_kv_heads, head_dim]
+ * (unit dim stride; typically the two halves of one [.., 2*head_dim] buffer).
+ * head_dim must be 64 or 128; num_q_heads / num_kv_heads must be 1..16.
+ */
+QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                         int32_t rows, int32_t num_q_heads, int32_t head_dim,
+                         const void* k_cache, int64_t k_block_stride, int64_t k_token_stride,
+                         int64_t k_head_stride, const void* v_cache, int64_t v_block_stride,
+                         int64_t v_token_stride, int64_t v_head_stride, int32_t num_blocks,
+                         int32_t page_size, int32_t num_kv_heads, const int32_t* indices,
+                         int64_t indices_row_stride, int32_t topk_width,
+                         const int32_t* block_table, int64_t table_row_stride,
+                         int32_t table_width, int32_t num_requests,
+                         const int32_t* token_to_req, const int32_t* valid_counts,
+                         const void* gate, int64_t gate_row_stride, int64_t gate_head_stride,
+                         int64_t gate_dim_stride, void* out, int64_t out_row_stride,
+                         int64_t out_head_stride, int32_t indices_are_physical,
+                         int32_t use_decode_kernel, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* QSA_B200_H_ */

@@ -1,0 +1,410 @@
+// C ABI of the QSA hot path (declared in include/qsa_b200.h): argument checks,
+// error reporting and dispatch to the kernel launchers.  Nothing here
+// allocates device memory or synchronises the host (except the explicit
+// qsa_device_error_poll).
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <tuple>
+
+#include "../../include/qsa_b200.h"
+#include "kernels.h"
+
+namespace qsa {
+
+namespace {
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(QSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Device-side error word, one per device (a __device__ variable is
+// instantiated per device context).
+__device__ int g_device_error = 0;
+
+constexpr int kMaxDevices = 64;
+int* g_err_ptr[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+std::mutex g_mu;
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int* device_error_word() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_err_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    g_err_ptr[dev] = static_cast<int*>(ptr);
+  }
+  return g_err_ptr[dev];
+}
+}  // namespace
+
+int num_sms() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sms[dev] = n;
+  }
+  return g_sms[dev];
+}
+
+cudaError_t set_attr_once(const void* fn, cudaFuncAttribute attr, int value) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int, int>> done;
+  const auto key = std::make_tuple(fn, static_cast<int>(attr), value, current_device());
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count(key)) return cudaSuccess;
+  }
+  const cudaError_t e = cudaFuncSetAttribute(fn, attr, value);
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lk(mu);
+    done.insert(key);
+  }
+  return e;
+}
+
+}  // namespace qsa
+
+using namespace qsa;
+
+extern "C" {
+
+const char* qsa_status_string(int status) {
+  switch (status) {
+    case QSA_OK: return "ok";
+    case QSA_ERR_INVALID: return "invalid argument";
+    case QSA_ERR_UNSUPPORTED: return "unsupported shape";
+    case QSA_ERR_WORKSPACE: return "workspace too small";
+    case QSA_ERR_CUDA: return "CUDA error";
+    case QSA_ERR_DEVICE: return "not an sm_100 device";
+    case QSA_ERR_TIMEOUT: return "device wait timed out";
+  }
+  return "unknown status";
+}
+
+const char* qsa_last_error(void) { return g_last_error; }
+
+const char* qsa_version(void) { return "qsa_b200 0.1.0 (sm_100a)"; }
+
+int qsa_device_check(void) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(QSA_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                major, minor);
+  return QSA_OK;
+}
+
+int qsa_device_error_poll(int32_t* error_bits) {
+  int* w = device_error_word();
+  if (w == nullptr) return fail(QSA_ERR_CUDA, "device error word unavailable");
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "reading device error word");
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing device error word");
+  }
+  if (error_bits) *error_bits = v;
+  return QSA_OK;
+}
+
+// ------------------------------------------------------------------ top-k
+static int topk_common(TopkParams& p, void* stream, const char* who) {
+  if (p.rows < 0 || p.width < 0) return fail(QSA_ERR_INVALID, "%s: negative rows/width", who);
+  if (p.rows == 0) return QSA_OK;
+  if (!p.scores || !p.lengths || !p.output)
+    return fail(QSA_ERR_INVALID, "%s: null scores/lengths/output", who);
+  if (p.score_row_stride < p.width)
+    return fail(QSA_ERR_INVALID, "%s: score row stride %lld < width %d", who,
+                (long long)p.score_row_stride, p.width);
+  if (p.width > topk_max_width())
+    return fail(QSA_ERR_UNSUPPORTED, "%s: score width %d exceeds %d", who, p.width,
+                topk_max_width());
+  p.vec4 = aligned(p.scores, 16) && (p.score_row_stride % 4 == 0);
+  int cluster = 0;
+  cudaError_t e = launch_topk(p, static_cast<cudaStream_t>(stream), &cluster);
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
+int qsa_topk_expand(const float* scores, int64_t score_row_stride, int32_t rows,
+                    int32_t score_width, const int32_t* lengths, const int64_t* positions,
+                    const int32_t* sequence_lengths, int32_t num_requests,
+                    const int32_t* token_to_req, const int32_t* table,
+                    int64_t table_row_stride, int32_t table_width, int32_t* output,
+                    int64_t output_row_stride, int64_t output_col_stride,
+                    int32_t output_width, int32_t* counts, int32_t ratio, int32_t page_size,
+                    int32_t physical, void* stream) {
+  if (ratio <= 0) return fail(QSA_ERR_INVALID, "qsa_topk_expand: ratio must be positive");
+  if (physical && page_size <= 0)
+    return fail(QSA_ERR_INVALID, "qsa_topk_expand: page_size must be positive");
+  if (rows > 0 && (!positions || !sequence_lengths || !token_to_req))
+    return fail(QSA_ERR_INVALID, "qsa_topk_expand: null metadata pointer");
+  if (physical && rows > 0 && !table)
+    return fail(QSA_ERR_INVALID, "qsa_topk_expand: physical output needs a table");
+  if (output_width < 0 || num_requests < 0)
+    return fail(QSA_ERR_INVALID, "qsa_topk_expand: negative output width / requests");
+  TopkParams p = {};
+  p.scores = scores;
+  p.score_row_stride = score_row_stride;
+  p.rows = rows;
+  p.width = score_width;
+  p.lengths = lengths;
+  p.positions = positions;
+  p.seq_lens = sequence_lengths;
+  p.num_requests = num_requests;
+  p.token_to_req = token_to_req;
+  p.table = table;
+  p.table_row_stride = table_row_stride;
+  p.table_width = physical ? table_width : 0;
+  p.output = output;
+  p.out_row_stride = output_row_stride;
+  p.out_col_stride = output_col_stride;
+  p.out_width = output_width;
+  p.counts = counts;
+  p.ratio = ratio;
+  p.page_size = physical ? page_size : 1;
+  p.physical = physical ? 1 : 0;
+  p.expand = 1;
+  p.topk = output_width / ratio;
+  return topk_common(p, stream, "qsa_topk_expand");
+}
+
+int qsa_topk(const float* scores, int64_t score_row_stride, int32_t rows, int32_t score_width,
+             const int32_t* lengths, int32_t* output, int64_t output_row_stride, int32_t topk,
+             void* stream) {
+  if (topk < 0) return fail(QSA_ERR_INVALID, "qsa_topk: negative topk");
+  TopkParams p = {};
+  p.scores = scores;
+  p.score_row_stride = score_row_stride;
+  p.rows = rows;
+  p.width = score_width;
+  p.lengths = lengths;
+  p.output = output;
+  p.out_row_stride = output_row_stride;
+  p.out_col_stride = 1;
+  p.out_width = topk;
+  p.ratio = 1;
+  p.page_size = 1;
+  p.expand = 0;
+  p.topk = topk;
+  return topk_common(p, stream, "qsa_topk");
+}
+
+// ---------------------------------------------------------------- indexer
+int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                       int32_t num_heads, int32_t head_dim, const void* k_cache,
+                       int64_t cache_block_stride, int64_t cache_token_stride,
+                       int32_t num_blocks, int32_t page_size, const int32_t* page_table,
+                       int64_t table_row_stride, int32_t table_width, int32_t num_requests,
+                       const int32_t* visible, const int32_t* query_start_loc,
+                       int32_t decode_query_len, int32_t max_query_len, int32_t query_offset,
+                       int32_t num_rows, const float* weights, int64_t weight_row_stride,
+                       int64_t weight_head_stride, float scale, float* logits,
+                       int64_t logits_row_stride, int32_t logits_width, void* stream) {
+  const char* who = "qsa_indexer_scores";
+  if (num_rows < 0 || logits_width < 0) return fail(QSA_ERR_INVALID, "%s: negative size", who);
+  if (num_rows == 0) return QSA_OK;
+  if (!q || !k_cache || !page_table || !visible || !logits)
+    return fail(QSA_ERR_INVALID, "%s: null pointer", who);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
+  const bool pow2 = num_heads > 0 && num_heads <= 8 && (num_heads & (num_heads - 1)) == 0;
+  if (!(pow2 || (num_heads % 8 == 0 && num_heads <= 128)))
+    return fail(QSA_ERR_UNSUPPORTED, "%s: %d heads (supported: 1,2,4,8 or a multiple of 8)",
+                who, num_heads);
+  if (page_size <= 0 || table_width < 0 || num_blocks < 0)
+    return fail(QSA_ERR_INVALID, "%s: bad page geometry", who);
+  if (!aligned(q, 16) || q_row_stride % 8 || q_head_stride % 8 || !aligned(k_cache, 16) ||
+      cache_block_stride % 8 || cache_token_stride % 8)
+    return fail(QSA_ERR_INVALID, "%s: q / key cache need 16-byte aligned rows", who);
+  if (query_start_loc == nullptr) {
+    if (decode_query_len <= 0 || num_rows % decode_query_len)
+      return fail(QSA_ERR_INVALID, "%s: %d decode rows not a multiple of query len %d", who,
+                  num_rows, decode_query_len);
+    if (decode_query_len * num_heads > 128)
+      return fail(QSA_ERR_UNSUPPORTED, "%s: decode_query_len*heads > 128", who);
+    if (query_offset != 0)
+      return fail(QSA_ERR_INVALID, "%s: decode rows start at offset 0", who);
+  } else if (num_requests <= 0 || max_query_len <= 0) {
+    return fail(QSA_ERR_INVALID, "%s: prefill needs requests and max_query_len", who);
+  }
+  IndexerParams p = {};
+  p.q = q;
+  p.q_row_stride = q_row_stride;
+  p.q_head_stride = q_head_stride;
+  p.heads = num_heads;
+  p.dim = head_dim;
+  p.k_cache = k_cache;
+  p.block_stride = cache_block_stride;
+  p.token_stride = cache_token_stride;
+  p.num_blocks = num_blocks;
+  p.page_size = page_size;
+  p.table = page_table;
+  p.table_row_stride = table_row_stride;
+  p.table_width = table_width;
+  p.num_requests = num_requests;
+  p.visible = visible;
+  p.query_start_loc = query_start_loc;
+  p.decode_query_len = decode_query_len;
+  p.max_query_len = max_query_len;
+  p.query_offset = query_offset;
+  p.num_rows = num_rows;
+  p.weights = weights;
+  p.w_row_stride = weight_row_stride;
+  p.w_head_stride = weight_head_stride;
+  p.scale = scale;
+  p.logits = logits;
+  p.logits_row_stride = logits_row_stride;
+  p.logits_width = logits_width;
+  p.err = device_error_word();
+  cudaError_t e = launch_indexer(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
+// -------------------------------------------------------------- attention
+size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
+                                            int32_t num_kv_heads, int32_t head_dim,
+                                            int32_t topk_width, int32_t use_decode_kernel) {
+  if (rows <= 0 || num_kv_heads <= 0) return 0;
+  return plan_attention(rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel)
+      .workspace_bytes;
+}
+
+int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                         int32_t rows, int32_t num_q_heads, int32_t head_dim,
+                         const void* k_cache, int64_t k_block_stride, int64_t k_token_stride,
+                         int64_t k_head_stride, const void* v_cache, int64_t v_block_stride,
+                         int64_t v_token_stride, int64_t v_head_stride, int32_t num_blocks,
+                         int32_t page_size, int32_t num_kv_heads, const int32_t* indices,
+                         int64_t indices_row_stride, int32_t topk_width,
+                         const int32_t* block_table, int64_t table_row_stride,
+                         int32_t table_width, int32_t num_requests,
+                         const int32_t* token_to_req, const int32_t* valid_counts,
+                         const void* gate, int64_t gate_row_stride, int64_t gate_head_stride,
+                         int64_t gate_dim_stride, void* out, int64_t out_row_stride,
+                         int64_t out_head_stride, int32_t indices_are_physical,
+                         int32_t use_decode_kernel, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  const char* who = "qsa_sparse_attention";
+  if (rows < 0 || topk_width < 0) return fail(QSA_ERR_INVALID, "%s: negative size", who);
+  if (rows == 0) return QSA_OK;
+  if (!q || !k_cache || !v_cache || !indices || !out)
+    return fail(QSA_ERR_INVALID, "%s: null pointer", who);
+  if (!indices_are_physical && (!block_table || !token_to_req))
+    return fail(QSA_ERR_INVALID, "%s: logical indices need block_table and token_to_req", who);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
+  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+    return fail(QSA_ERR_INVALID, "%s: %d query heads not a multiple of %d kv heads", who,
+                num_q_heads, num_kv_heads);
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 16)
+    return fail(QSA_ERR_UNSUPPORTED, "%s: GQA group %d > 16", who, group);
+  if (page_size <= 0 || num_blocks < 0) return fail(QSA_ERR_INVALID, "%s: bad page geometry", who);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || k_block_stride % 8 ||
+      k_token_stride % 8 || k_head_stride % 8 || v_block_stride % 8 || v_token_stride % 8 ||
+      v_head_stride % 8)
+    return fail(QSA_ERR_INVALID, "%s: K/V cache rows must be 16-byte aligned", who);
+  if (!aligned(q, 4) || q_row_stride % 2 || q_head_stride % 2 || !aligned(out, 4) ||
+      out_row_stride % 2 || out_head_stride % 2)
+    return fail(QSA_ERR_INVALID, "%s: q / out rows must be 4-byte aligned", who);
+  const AttnPlan plan =
+      plan_attention(rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel);
+  if (plan.workspace_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.workspace_bytes))
+    return fail(QSA_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", who, workspace_bytes,
+                plan.workspace_bytes);
+  if (plan.workspace_bytes > 0 && !aligned(workspace, 256))
+    return fail(QSA_ERR_INVALID, "%s: workspace must be 256-byte aligned", who);
+  AttnParams p = {};
+  p.q = q;
+  p.q_row_stride = q_row_stride;
+  p.q_head_stride = q_head_stride;
+  p.rows = rows;
+  p.q_heads = num_q_heads;
+  p.dim = head_dim;
+  p.k_cache = k_cache;
+  p.k_block_stride = k_block_stride;
+  p.k_token_stride = k_token_stride;
+  p.k_head_stride = k_head_stride;
+  p.v_cache = v_cache;
+  p.v_block_stride = v_block_stride;
+  p.v_token_stride = v_token_stride;
+  p.v_head_stride = v_head_stride;
+  p.num_blocks = num_blocks;
+  p.page_size = page_size;
+  p.kv_heads = num_kv_heads;
+  p.indices = indices;
+  p.indices_row_stride = indices_row_stride;
+  p.topk_width = topk_width;
+  p.block_table = block_table;
+  p.table_row_stride = table_row_stride;
+  p.table_width = table_width;
+  p.num_requests = num_requests;
+  p.token_to_req = token_to_req;
+  p.valid_counts = valid_counts;
+  p.gate = gate;
+  p.gate_row_stride = gate_row_stride;
+  p.gate_head_stride = gate_head_stride;
+  p.gate_dim_stride = gate_dim_stride;
+  p.out = out;
+  p.out_row_stride = out_row_stride;
+  p.out_head_stride = out_head_stride;
+  p.scale_log2 = static_cast<float>(std::pow(static_cast<double>(head_dim), -0.5) *
+                                    1.4426950408889634);
+  p.physical = indices_are_physical ? 1 : 0;
+  p.kv_fused = (static_cast<const char*>(v_cache) ==
+                static_cast<const char*>(k_cache) + 2 * head_dim) &&
+               k_block_stride == v_block_stride && k_token_stride == v_token_stride &&
+               k_head_stride == v_head_stride;
+  p.splits = plan.splits;
+  if (plan.splits > 1) {
+    const size_t o_bytes =
+        static_cast<size_t>(plan.splits) * rows * num_q_heads * head_dim * sizeof(float);
+    p.part_o = static_cast<float*>(workspace);
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                          ((o_bytes + 255) & ~static_cast<size_t>(255)));
+  }
+  p.err = device_error_word();
+  cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
+}  // extern "C"

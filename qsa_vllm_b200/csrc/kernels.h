@@ -1,0 +1,107 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernel
+// translation units.  Plain structs of pointers, strides and sizes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qsa {
+
+// ----------------------------------------------------------------- top-k
+struct TopkParams {
+  const float* scores;
+  int64_t score_row_stride;
+  int rows, width;
+  const int32_t* lengths;
+  const int64_t* positions;
+  const int32_t* seq_lens;
+  int num_requests;
+  const int32_t* token_to_req;
+  const int32_t* table;
+  int64_t table_row_stride;
+  int table_width;
+  int32_t* output;
+  int64_t out_row_stride, out_col_stride;
+  int out_width;
+  int32_t* counts;
+  int ratio, page_size;
+  int physical;   // expansion maps tokens to slots through `table`
+  int expand;     // 0: plain ids (torch.ops...topk), 1: expanded tokens
+  int topk;       // selected blocks per row
+  int slice_cap;  // keys held in shared memory per CTA
+  int vec4;       // rows are 16-byte aligned: float4 loads
+};
+// Chooses the cluster width and launches.  Returns cudaError_t.
+cudaError_t launch_topk(const TopkParams& p, cudaStream_t stream, int* plan_cluster);
+// Largest score width the shared-memory-resident select supports.
+int topk_max_width();
+
+// --------------------------------------------------------------- indexer
+struct IndexerParams {
+  const void* q;
+  int64_t q_row_stride, q_head_stride;
+  int heads, dim;
+  const void* k_cache;
+  int64_t block_stride, token_stride;
+  int num_blocks, page_size;
+  const int32_t* table;
+  int64_t table_row_stride;
+  int table_width, num_requests;
+  const int32_t* visible;
+  const int32_t* query_start_loc;  // nullptr: uniform decode
+  int decode_query_len, max_query_len, query_offset, num_rows;
+  const float* weights;
+  int64_t w_row_stride, w_head_stride;
+  float scale;
+  float* logits;
+  int64_t logits_row_stride;
+  int logits_width;
+  int* err;
+};
+cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream);
+
+// ------------------------------------------------------------- attention
+struct AttnParams {
+  const void* q;
+  int64_t q_row_stride, q_head_stride;
+  int rows, q_heads, dim;
+  const void* k_cache;
+  int64_t k_block_stride, k_token_stride, k_head_stride;
+  const void* v_cache;
+  int64_t v_block_stride, v_token_stride, v_head_stride;
+  int num_blocks, page_size, kv_heads;
+  const int32_t* indices;
+  int64_t indices_row_stride;
+  int topk_width;
+  const int32_t* block_table;
+  int64_t table_row_stride;
+  int table_width, num_requests;
+  const int32_t* token_to_req;
+  const int32_t* valid_counts;
+  const void* gate;
+  int64_t gate_row_stride, gate_head_stride, gate_dim_stride;
+  void* out;
+  int64_t out_row_stride, out_head_stride;
+  float scale_log2;  // head_dim^-0.5 * log2(e), rounded once to fp32 (ops/qsa.py:176)
+  int physical;
+  int kv_fused;     // V row directly follows the K row: one copy per token
+  int splits;       // split-K factor per (row, kv head)
+  float* part_o;    // [splits, rows, q_heads, dim] fp32 (splits > 1)
+  float* part_lse;  // [splits, rows, q_heads] fp32
+  int* err;
+};
+struct AttnPlan {
+  int splits;
+  size_t workspace_bytes;
+};
+AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
+                        int use_decode_kernel);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
+
+int num_sms();
+// cudaFuncSetAttribute(fn, attr, value) once per (function, attribute, device);
+// later launches (including ones under CUDA-graph capture) skip the call.
+cudaError_t set_attr_once(const void* fn, cudaFuncAttribute attr, int value);
+
+}  // namespace qsa

@@ -1,0 +1,196 @@
+"""Indexer scoring + fused top-k selection (drop-in for the reference ops/indexer.py).
+
+Host logic mirrors the reference (ops/indexer.py:227-393): decode rows are
+scored against the column bucket chosen by ``graph_dispatch`` and prefill rows
+against ``round64(ceil(max_seq_len / ratio))`` columns, both through an fp32
+logits workspace chunked by ``QSA_INDEXER_WORKSPACE_MB`` (default 64 MiB),
+each chunk followed by the top-k/expansion op.  The scoring itself is the
+sm_100a ``qsa_indexer_scores`` kernel; selection is ``topk_expand``.
+
+Two optional keyword arguments extend the reference signature: ``weights``
+(fp32 per-row head weights, ``[rows, heads]``, broadcastable) and ``scale``
+(default ``head_dim ** -0.5``).  Without them the math is the reference's
+(unit head weights, ops/indexer.py:107,213).
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+
+from . import _lib
+from .graph_dispatch import decode_logits_columns
+from .topk import topk_expand as _topk_expand
+
+_INDEXER_WORKSPACE_BYTES = int(os.environ.get("QSA_INDEXER_WORKSPACE_MB", "64")) * 1024 * 1024
+
+
+def _cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+def indexer_scores(q: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Tensor,
+                   visible: torch.Tensor, logits: torch.Tensor, *,
+                   decode_query_len: int = 1, query_start_loc: torch.Tensor | None = None,
+                   max_query_len: int = 0, query_offset: int = 0, num_rows: int | None = None,
+                   weights: torch.Tensor | None = None, scale: float | None = None) -> None:
+    """Write ``logits[r - query_offset, c]`` for the packed rows of this call.
+
+    Decode (``query_start_loc is None``): ``q`` holds ``requests * decode_query_len``
+    rows and ``page_table`` one row per request.  Prefill: ``q``/``visible`` are
+    the full packed tensors indexed by absolute row, the call covers rows
+    ``[query_offset, query_offset + num_rows)`` (as ``_prefill_logits``,
+    ops/indexer.py:282-302).
+    """
+    rows = q.shape[0] if num_rows is None else num_rows
+    if rows == 0:
+        return
+    _lib.ensure_device(q.device)
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16:
+        raise TypeError("indexer q and key cache must be bfloat16")
+    if logits.dtype != torch.float32 or logits.stride(-1) != 1:
+        raise TypeError("logits must be float32 with unit column stride")
+    if page_table.dtype != torch.int32 or visible.dtype != torch.int32:
+        raise TypeError("page_table and visible must be int32")
+    if q.stride(-1) != 1 or k_cache.stride(-1) != 1:
+        raise ValueError("q and k_cache need a unit head-dim stride")
+    w_ptr, w_rs, w_hs = None, 0, 0
+    if weights is not None:
+        if weights.dtype != torch.float32:
+            raise TypeError("weights must be float32")
+        w = weights.expand(q.shape[0], q.shape[1])
+        w_ptr, w_rs, w_hs = w.data_ptr(), w.stride(0), w.stride(1)
+    dim = q.shape[2]
+    if scale is None:
+        scale = float(np.float32(dim ** -0.5))
+    qsl = query_start_loc
+    if qsl is not None and qsl.dtype != torch.int32:
+        raise TypeError("query_start_loc must be int32")
+    lib = _lib.load_library()
+    with torch.cuda.device(q.device):
+        _lib.check(lib.qsa_indexer_scores(
+            q.data_ptr(), q.stride(0), q.stride(1), q.shape[1], dim,
+            k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.shape[0],
+            k_cache.shape[1], page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+            page_table.shape[0] if qsl is None else qsl.numel() - 1,
+            visible.data_ptr(), None if qsl is None else qsl.data_ptr(),
+            int(decode_query_len), int(max_query_len), int(query_offset), int(rows),
+            w_ptr, w_rs, w_hs, float(scale), logits.data_ptr(), logits.stride(0),
+            logits.shape[1], _lib.stream_ptr(q.device)), "indexer_scores")
+
+
+def qsa_select_paged_decode(q, k_cache, page_table, visible_blocks, token_topk, compress_ratio,
+                            decode_query_len, out, max_seq_len, *, query_positions,
+                            sequence_lengths, token_to_req, main_block_table=None,
+                            main_page_size=1, valid_counts_out=None, weights=None, scale=None):
+    """Score decode queries and write the expanded selection (ops/indexer.py:227-279)."""
+    num_requests = q.shape[0] // decode_query_len
+    columns = decode_logits_columns(max_seq_len, compress_ratio,
+                                    page_table.shape[1] * k_cache.shape[1])
+    requests_per_chunk = max(1, _INDEXER_WORKSPACE_BYTES // (columns * 4 * decode_query_len))
+    workspace_rows = min(num_requests, requests_per_chunk) * decode_query_len
+    logits_workspace = torch.empty((workspace_rows, columns), dtype=torch.float32,
+                                   device=q.device)
+    for first in range(0, num_requests, requests_per_chunk):
+        last = min(first + requests_per_chunk, num_requests)
+        r0, r1 = first * decode_query_len, last * decode_query_len
+        logits = logits_workspace[:r1 - r0]
+        indexer_scores(q[r0:r1], k_cache, page_table[first:last], visible_blocks[r0:r1], logits,
+                       decode_query_len=decode_query_len,
+                       weights=None if weights is None else weights[r0:r1], scale=scale)
+        _topk_expand(
+            logits, visible_blocks[r0:r1], query_positions[r0:r1], sequence_lengths,
+            token_to_req[r0:r1], out[r0:r1], compress_ratio,
+            main_block_table=main_block_table, main_page_size=main_page_size,
+            valid_counts_out=(valid_counts_out[r0:r1] if valid_counts_out is not None else None))
+
+
+def _prefill_logits(q, k_cache, page_table, query_start_loc, visible_blocks, logits_workspace,
+                    max_query_len, logits_width, query_offset, num_queries, *, weights=None,
+                    scale=None):
+    """Score packed prefill rows [query_offset, query_offset+num_queries) (ops/indexer.py:282-302)."""
+    logits = logits_workspace[:num_queries * logits_width].view(num_queries, logits_width)
+    indexer_scores(q, k_cache, page_table, visible_blocks, logits,
+                   query_start_loc=query_start_loc, max_query_len=max_query_len,
+                   query_offset=query_offset, num_rows=num_queries, weights=weights, scale=scale)
+    return logits
+
+
+def qsa_select_paged_prefill(q, k_cache, page_table, query_start_loc, visible_blocks, token_topk,
+                             compress_ratio, max_query_len, out, max_seq_len, *, query_positions,
+                             sequence_lengths, token_to_req, main_block_table=None,
+                             main_page_size=1, valid_counts_out=None, weights=None, scale=None):
+    """Packed prefill scoring and fused selection write-out (ops/indexer.py:305-343)."""
+    rows = q.shape[0]
+    columns = page_table.shape[1] * k_cache.shape[1]
+    logits_width = _cdiv(_cdiv(max_seq_len, compress_ratio), 64) * 64
+    logits_width = min(max(64, logits_width), columns)
+    rows_per_chunk = max(1, _INDEXER_WORKSPACE_BYTES // (logits_width * 4))
+    logits_workspace = torch.empty(min(rows, rows_per_chunk) * logits_width,
+                                   dtype=torch.float32, device=q.device)
+    for start in range(0, rows, rows_per_chunk):
+        end = min(start + rows_per_chunk, rows)
+        logits = _prefill_logits(q, k_cache, page_table, query_start_loc, visible_blocks,
+                                 logits_workspace, max_query_len, logits_width,
+                                 query_offset=start, num_queries=end - start,
+                                 weights=weights, scale=scale)
+        _topk_expand(
+            logits, visible_blocks[start:end], query_positions[start:end], sequence_lengths,
+            token_to_req[start:end], out[start:end], compress_ratio,
+            main_block_table=main_block_table, main_page_size=main_page_size,
+            valid_counts_out=(valid_counts_out[start:end] if valid_counts_out is not None
+                              else None))
+
+
+def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, sequence_lengths,
+                        token_topk, compress_ratio, out=None, *, query_start_loc, max_query_len,
+                        max_seq_len, num_decodes=0, num_decode_tokens=0, decode_query_len=1,
+                        visible_blocks=None, main_block_table=None, main_page_size=1,
+                        valid_counts_out=None, weights=None, scale=None):
+    """Select blocks and write expanded decode/prefill tokens (ops/indexer.py:346-393).
+
+    Decode rows come first (``[:num_decode_tokens]``, one page-table row per
+    decode request), then packed prefill rows.
+    """
+    rows = q.shape[0]
+    if out is None:
+        out = torch.empty((rows, token_topk + compress_ratio - 1), dtype=torch.int32,
+                          device=q.device)
+    if not rows:
+        return out
+    if visible_blocks is None:
+        safe_requests = token_to_req.clamp_min(0).long()
+        visible_blocks = torch.minimum(
+            (query_positions + 1) // compress_ratio,
+            sequence_lengths.index_select(0, safe_requests) // compress_ratio,
+        ).to(torch.int32)
+        visible_blocks = torch.where(token_to_req >= 0, visible_blocks, 0)
+    if num_decode_tokens:
+        qsa_select_paged_decode(
+            q[:num_decode_tokens], k_cache, page_table[:num_decodes],
+            visible_blocks[:num_decode_tokens], token_topk, compress_ratio, decode_query_len,
+            out[:num_decode_tokens], max_seq_len,
+            query_positions=query_positions[:num_decode_tokens],
+            sequence_lengths=sequence_lengths, token_to_req=token_to_req[:num_decode_tokens],
+            main_block_table=main_block_table, main_page_size=main_page_size,
+            valid_counts_out=(valid_counts_out[:num_decode_tokens]
+                              if valid_counts_out is not None else None),
+            weights=None if weights is None else weights[:num_decode_tokens], scale=scale)
+    if num_decode_tokens < rows:
+        qsa_select_paged_prefill(
+            q[num_decode_tokens:], k_cache, page_table[num_decodes:],
+            query_start_loc[num_decodes:], visible_blocks[num_decode_tokens:], token_topk,
+            compress_ratio, max_query_len, out[num_decode_tokens:], max_seq_len,
+            query_positions=query_positions[num_decode_tokens:],
+            sequence_lengths=sequence_lengths, token_to_req=token_to_req[num_decode_tokens:],
+            main_block_table=main_block_table, main_page_size=main_page_size,
+            valid_counts_out=(valid_counts_out[num_decode_tokens:]
+                              if valid_counts_out is not None else None),
+            weights=None if weights is None else weights[num_decode_tokens:], scale=scale)
+    return out
+
+
+__all__ = ["indexer_scores", "qsa_select_paged_decode", "qsa_select_paged_prefill",
+           "select_paged_tokens"]

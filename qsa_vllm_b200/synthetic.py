@@ -1,0 +1,193 @@
+"""Seeded synthetic QSA layer inputs with the shapes of the benchmark configurations.
+
+No dataset is involved: every input is drawn from a seeded generator with the
+distributions the benchmark specifies (q / K / V / index keys N(0,1) bf16, q
+scaled by head_dim^-0.5, head weights U(0,1)), on paged caches whose block
+tables are seeded random permutations of the physical pool (so consecutive
+logical pages land on scattered physical pages, as in a fragmented cache).
+
+Layouts match what the reference plugin receives from vLLM:
+  * main cache ``kv``: bf16 ``[num_blocks, page, H_kv, 2*d]``; ``k_cache`` /
+    ``v_cache`` are the two halves of the last dim (backend.py:148-153);
+  * index-key cache: bf16 ``[num_index_blocks, index_page, 1, d_i]`` (one
+    compressed key per ``ratio`` tokens) with its own block table;
+  * decode rows are the last token of each request: position = seq_len - 1.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+# name -> configuration ("cfg2_32k" is the headline decode point)
+CONFIGS: dict[str, dict] = {
+    "cfg0": dict(batch=4, seq_len=2048, hq=16, hkv=2, d=128, hi=4, di=64, page=16,
+                 num_blocks=512, token_topk=512, ratio=4),
+    "cfg1": dict(batch=2, seq_len=8192, new_tokens=4096, hq=16, hkv=2, d=128, hi=4, di=64,
+                 page=16, token_topk=1024, ratio=4),
+    "cfg2": dict(batch=64, seq_len=(8192, 32768), hq=32, hkv=4, d=128, hi=8, di=64, page=64,
+                 token_topk=2048, ratio=4),
+    "cfg2_32k": dict(batch=64, seq_len=32768, hq=32, hkv=4, d=128, hi=8, di=64, page=64,
+                     token_topk=2048, ratio=4),
+    "cfg3": dict(batch=8, seq_len=131072, hq=32, hkv=4, d=128, hi=8, di=64, page=64,
+                 token_topk=2048, ratio=4),
+}
+
+
+@dataclass
+class SyntheticQSA:
+    """One QSA layer's inputs for a decode or chunked-prefill step."""
+    name: str
+    ratio: int
+    token_topk: int
+    page_size: int
+    seq_lens: torch.Tensor          # int32 [B]
+    positions: torch.Tensor         # int64 [rows]
+    token_to_req: torch.Tensor      # int32 [rows]
+    query_start_loc: torch.Tensor   # int32 [B+1]
+    q: torch.Tensor                 # bf16 [rows, H_q, d]
+    gate: torch.Tensor              # bf16 [rows, H_q, d]
+    kv: torch.Tensor                # bf16 [blocks, page, H_kv, 2d]
+    block_table: torch.Tensor       # int32 [B, width]
+    index_q: torch.Tensor           # bf16 [rows, H_i, d_i]
+    index_weights: torch.Tensor | None  # fp32 [rows, H_i]
+    index_scale: float
+    index_cache: torch.Tensor       # bf16 [index_blocks, page, 1, d_i]
+    index_table: torch.Tensor       # int32 [B, index_width]
+    is_decode: bool = True
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def d(self) -> int:
+        return self.q.shape[2]
+
+    @property
+    def k_cache(self) -> torch.Tensor:
+        return self.kv[..., : self.d]
+
+    @property
+    def v_cache(self) -> torch.Tensor:
+        return self.kv[..., self.d:]
+
+    @property
+    def rows(self) -> int:
+        return self.q.shape[0]
+
+    @property
+    def max_seq_len(self) -> int:
+        return int(self.seq_lens.max())
+
+    @property
+    def max_query_len(self) -> int:
+        q = self.query_start_loc
+        return int((q[1:] - q[:-1]).max())
+
+    def shard_heads(self, tp_size: int, tp_rank: int) -> "SyntheticQSA":
+        """This rank's view under head (tensor-parallel) sharding: query heads and
+        KV heads split ``//tp`` (attention.py:148-150); when tp exceeds the KV
+        head count each rank keeps the one KV head its query heads use.  The
+        indexer and its caches are replicated on every rank (cache.py:6-7)."""
+        from .sharding import head_shard
+        qs, ks = head_shard(self.q.shape[1], self.kv.shape[2], tp_size, tp_rank)
+        kv = self.kv[:, :, ks].contiguous()
+        return SyntheticQSA(
+            name=f"{self.name}/tp{tp_size}r{tp_rank}", ratio=self.ratio,
+            token_topk=self.token_topk, page_size=self.page_size, seq_lens=self.seq_lens,
+            positions=self.positions, token_to_req=self.token_to_req,
+            query_start_loc=self.query_start_loc, q=self.q[:, qs].contiguous(),
+            gate=self.gate[:, qs].contiguous(), kv=kv, block_table=self.block_table,
+            index_q=self.index_q, index_weights=self.index_weights,
+            index_scale=self.index_scale, index_cache=self.index_cache,
+            index_table=self.index_table, is_decode=self.is_decode, extra=dict(self.extra))
+
+
+def _tables(gen: torch.Generator, pages_per_req: list[int], device) -> tuple[torch.Tensor, int]:
+    total = sum(pages_per_req)
+    perm = torch.randperm(total, generator=gen).to(torch.int32)
+    width = max(pages_per_req)
+    table = torch.full((len(pages_per_req), width), -1, dtype=torch.int32)
+    off = 0
+    for r, n in enumerate(pages_per_req):
+        table[r, :n] = perm[off:off + n]
+        off += n
+    return table.to(device), total
+
+
+def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
+                  batch: int | None = None, seq_len: int | tuple | None = None,
+                  head_weights: bool = True, dtype_gen_device: str | None = None,
+                  **overrides) -> SyntheticQSA:
+    """Build the inputs of configuration ``name`` (see ``CONFIGS``).
+
+    ``batch`` / ``seq_len`` / other keys override the configuration (tests use
+    small versions of the same shapes).  Random tensors are drawn on
+    ``device`` with a generator seeded by ``seed``; metadata is built on the CPU.
+    ``head_weights=False`` gives the reference's unit head weights.
+    """
+    cfg = dict(CONFIGS[name])
+    if batch is not None:
+        cfg["batch"] = batch
+    if seq_len is not None:
+        cfg["seq_len"] = seq_len
+    cfg.update(overrides)
+    device = torch.device(device)
+    cpu = torch.Generator().manual_seed(seed)
+    B, ratio, page = cfg["batch"], cfg["ratio"], cfg["page"]
+    sl = cfg["seq_len"]
+    if isinstance(sl, tuple):
+        seq_lens = torch.randint(sl[0], sl[1] + 1, (B,), generator=cpu).to(torch.int32)
+    else:
+        seq_lens = torch.full((B,), int(sl), dtype=torch.int32)
+    new = cfg.get("new_tokens")
+    is_decode = new is None
+    if is_decode:
+        q_lens = torch.ones(B, dtype=torch.int32)
+    else:
+        q_lens = torch.full((B,), int(new), dtype=torch.int32)
+    qsl = torch.zeros(B + 1, dtype=torch.int32)
+    qsl[1:] = torch.cumsum(q_lens, 0)
+    rows = int(qsl[-1])
+    token_to_req = torch.repeat_interleave(torch.arange(B, dtype=torch.int32), q_lens.long())
+    positions = torch.cat([torch.arange(int(L) - int(n), int(L), dtype=torch.int64)
+                           for L, n in zip(seq_lens, q_lens)])
+
+    main_pages = [-(-int(L) // page) for L in seq_lens]
+    if "num_blocks" in cfg and sum(main_pages) <= cfg["num_blocks"]:
+        main_pages_pool = cfg["num_blocks"]
+    else:
+        main_pages_pool = sum(main_pages)
+    perm = torch.randperm(main_pages_pool, generator=cpu).to(torch.int32)
+    width = max(main_pages)
+    block_table = torch.full((B, width), -1, dtype=torch.int32)
+    off = 0
+    for r, n in enumerate(main_pages):
+        block_table[r, :n] = perm[off:off + n]
+        off += n
+    index_pages = [max(1, -(-(int(L) // ratio) // page)) for L in seq_lens]
+    index_table, index_pool = _tables(cpu, index_pages, "cpu")
+
+    gdev = torch.Generator(device=device).manual_seed(seed + 1)
+    hq, hkv, d, hi, di = cfg["hq"], cfg["hkv"], cfg["d"], cfg["hi"], cfg["di"]
+
+    def randn(*shape, scale=1.0):
+        x = torch.randn(*shape, generator=gdev, device=device, dtype=torch.bfloat16)
+        return x if scale == 1.0 else (x.float() * scale).to(torch.bfloat16)
+
+    kv = randn(main_pages_pool, page, hkv, 2 * d)
+    q = randn(rows, hq, d, scale=d ** -0.5)
+    gate = randn(rows, hq, d)
+    index_cache = randn(index_pool, page, 1, di)
+    index_q = randn(rows, hi, di, scale=di ** -0.5)
+    weights = (torch.rand(rows, hi, generator=gdev, device=device, dtype=torch.float32)
+               if head_weights else None)
+    return SyntheticQSA(
+        name=name, ratio=ratio, token_topk=cfg["token_topk"], page_size=page,
+        seq_lens=seq_lens.to(device), positions=positions.to(device),
+        token_to_req=token_to_req.to(device), query_start_loc=qsl.to(device), q=q, gate=gate,
+        kv=kv, block_table=block_table.to(device), index_q=index_q, index_weights=weights,
+        index_scale=di ** -0.5, index_cache=index_cache, index_table=index_table.to(device),
+        is_decode=is_decode, extra={"config": cfg})
+
+
+__all__ = ["CONFIGS", "SyntheticQSA", "make_workload"]

@@ -1,0 +1,261 @@
+"""Host-side tests that need no GPU: the C-ABI library, graph buckets, sharding,
+and the indexer/top-k chunking logic (kernels replaced by the CPU oracle)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qsa_oracle as O
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "qsa_b200.h"
+
+
+def header_functions() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"QSA_API\s+[\w\s\*]+?\b(qsa_\w+)\s*\(", text)
+
+
+def test_header_declares_the_three_stages():
+    names = header_functions()
+    for n in ("qsa_indexer_scores", "qsa_topk_expand", "qsa_topk", "qsa_sparse_attention",
+              "qsa_sparse_attention_workspace_bytes", "qsa_last_error", "qsa_status_string"):
+        assert n in names
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    from qsa_vllm_b200 import _lib
+    lib = _lib.load_library()
+    for name in header_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    raw = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in header_functions():
+        getattr(raw, name)
+
+
+def test_host_only_entry_points():
+    from qsa_vllm_b200 import _lib
+    lib = _lib.load_library()
+    assert b"sm_100a" in lib.qsa_version()
+    assert lib.qsa_status_string(0) == b"ok"
+    assert lib.qsa_status_string(3) == b"workspace too small"
+    # rows == 0 is a no-op that never touches the device
+    assert lib.qsa_topk_expand(None, 0, 0, 0, None, None, None, 0, None, None, 0, 0, None, 0, 1,
+                               7, None, 4, 16, 1, None) == 0
+    assert lib.qsa_sparse_attention(None, 0, 0, 0, 32, 128, None, 0, 0, 0, None, 0, 0, 0, 0, 16,
+                                    4, None, 0, 0, None, 0, 0, 0, None, None, None, 0, 0, 0, None,
+                                    0, 0, 1, 1, None, 0, None) == 0
+
+
+def test_argument_errors_are_reported_not_launched():
+    from qsa_vllm_b200 import _lib
+    lib = _lib.load_library()
+    st = lib.qsa_topk_expand(None, 0, 1, 8, None, None, None, 0, None, None, 0, 0, None, 0, 1,
+                             7, None, 0, 16, 1, None)
+    assert st == 1 and b"ratio" in lib.qsa_last_error()
+    st = lib.qsa_indexer_scores(1024, 64, 64, 4, 96, 1024, 0, 0, 1, 16, 1024, 0, 1, 1, 1024,
+                                None, 1, 1, 0, 1, None, 0, 0, 1.0, 1024, 0, 8, None)
+    assert st == 2 and b"head_dim" in lib.qsa_last_error()
+    st = lib.qsa_sparse_attention(1024, 0, 0, 1, 48, 128, 1024, 0, 0, 0, 1024, 0, 0, 0, 1, 16,
+                                  2, 1024, 0, 8, None, 0, 0, 0, None, None, None, 0, 0, 0, 1024,
+                                  0, 0, 1, 1, None, 0, None)
+    assert st == 2 and b"group" in lib.qsa_last_error()
+    with pytest.raises(_lib.QSAError):
+        _lib.check(1, "probe")
+
+
+def test_attention_workspace_query_is_deterministic():
+    from qsa_vllm_b200.qsa import attention_workspace_bytes
+    a = attention_workspace_bytes(64, 32, 4, 128, 2051, True)
+    assert a == attention_workspace_bytes(64, 32, 4, 128, 2051, True)
+    assert attention_workspace_bytes(8192, 16, 2, 128, 1027, False) == 0
+
+
+def test_operators_fail_loudly_without_a_gpu():
+    from qsa_vllm_b200 import _lib
+    from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    kv = torch.zeros(4, 16, 1, 256, dtype=torch.bfloat16)
+    with pytest.raises(_lib.QSAError):
+        qsa_sparse_paged_attention(q, kv[..., :128], kv[..., 128:],
+                                   torch.zeros(2, 7, dtype=torch.int32),
+                                   torch.zeros(1, 1, dtype=torch.int32),
+                                   torch.zeros(2, dtype=torch.int32), indices_are_physical=True)
+
+
+# ------------------------------------------------------------ graph buckets
+def test_decode_column_buckets():
+    from qsa_vllm_b200 import graph_dispatch as gd
+    assert gd.decode_column_bucket(131072) == 32768
+    assert gd.decode_column_bucket(131073 + 3) == 0
+    assert gd.decode_logits_columns(4096, 4, 8192) == 8192        # bucket clipped to capacity
+    assert gd.decode_logits_columns(524288, 4, 131072) == 131072  # full capacity
+    with gd.capture_column_scope(0):
+        assert gd.decode_logits_columns(10, 4, 5000) == 5000
+    with gd.capture_column_scope(32768):
+        assert gd.decode_logits_columns(10 ** 7, 4, 40000) == 32768
+    assert gd.decode_logits_columns(4096, 4, 40000) == 32768
+
+
+def test_graph_dispatch_patch_with_fake_vllm():
+    from dataclasses import dataclass
+    from types import SimpleNamespace
+
+    from qsa_vllm_b200 import graph_dispatch as gd
+
+    FULL, PIECE = "FULL", "PIECEWISE"
+
+    @dataclass(frozen=True)
+    class Desc:
+        cg_mode: str
+        num_tokens: int
+
+    class GraphManager:
+        def capture(self, create_forward_fn, progress_bar_desc=""):
+            return [create_forward_fn(d, False)("run") for d in self._capture_descs[FULL]]
+
+    class ModelGraphManager(GraphManager):
+        def _init_candidates(self):
+            self._capture_descs = {FULL: [Desc(FULL, 8)], PIECE: [Desc(PIECE, 8)]}
+
+        def dispatch(self, n):
+            return Desc(FULL, n)
+
+    class Runner:
+        def gather_batch_req_state(self, scheduler_output, dummy_run):
+            return scheduler_output, True
+
+    gd.install_short_decode_dispatch(ModelGraphManager, GraphManager, Runner, FULL, Desc)
+    m = ModelGraphManager()
+    m._init_candidates()
+    cols = sorted(d.qsa_columns for d in m._capture_descs[FULL])
+    assert cols == [0, 32768]
+    seen = m.capture(lambda desc, warm: (lambda mode: gd.decode_logits_columns(10, 4, 50000)))
+    assert sorted(seen) == [32768, 50000]
+    runner = Runner()
+    runner.req_states = SimpleNamespace(num_computed_tokens_np=np.array([100, 600000]))
+    batch = SimpleNamespace(idx_mapping_np=np.array([0]), num_scheduled_tokens=np.array([1]))
+    runner.gather_batch_req_state(batch, False)
+    assert gd.runtime_columns() == 32768 and m.dispatch(8).qsa_columns == 32768
+    batch.idx_mapping_np = np.array([1])
+    runner.gather_batch_req_state(batch, False)
+    assert gd.runtime_columns() == 0 and m.dispatch(8).qsa_columns == 0
+
+
+# ----------------------------------------------------------------- sharding
+def test_head_shard_rule():
+    from qsa_vllm_b200.sharding import head_shard
+    assert head_shard(32, 4, 1, 0) == (slice(0, 32), slice(0, 4))
+    assert head_shard(32, 4, 2, 1) == (slice(16, 32), slice(2, 4))
+    assert head_shard(32, 4, 4, 3) == (slice(24, 32), slice(3, 4))
+    # tp > kv heads: KV heads replicated, each rank keeps the one its queries use
+    assert [head_shard(32, 4, 8, r)[1] for r in range(8)] == [slice(r // 2, r // 2 + 1)
+                                                            for r in range(8)]
+    with pytest.raises(ValueError):
+        head_shard(32, 4, 3, 0)
+
+
+def _sharded_worker(rank, world, port, result_path):
+    import torch.distributed as dist
+    from qsa_vllm_b200.sharding import head_shard
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        g = torch.Generator().manual_seed(0)
+        rows, hq, hkv, d, page, nblk = 4, 16, 2, 64, 16, 12
+        kv = torch.randn(nblk, page, hkv, 2 * d, generator=g).to(torch.bfloat16)
+        q = (torch.randn(rows, hq, d, generator=g) * 0.2).to(torch.bfloat16)
+        idx = torch.randint(-1, nblk * page, (rows, 35), generator=g).to(torch.int32)
+        t2r = torch.zeros(rows, dtype=torch.int32)
+        table = torch.zeros(1, 1, dtype=torch.int32)
+        qs, ks = head_shard(hq, hkv, world, rank)
+        part = O.sparse_attention(q[:, qs], kv[:, :, ks, :d], kv[:, :, ks, d:], idx, table, t2r,
+                                  indices_are_physical=True, use_decode_kernel=True,
+                                  block_n=32, num_splits=1)
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)       # test-only: reassemble the head shards
+        if rank == 0:
+            full = O.sparse_attention(q, kv[..., :d], kv[..., d:], idx, table, t2r,
+                                      indices_are_physical=True, use_decode_kernel=True,
+                                      block_n=32, num_splits=1)
+            ok = torch.equal(torch.cat(parts, dim=1), full)
+            Path(result_path).write_text("ok" if ok else "mismatch")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_sharded_attention_two_gloo_ranks(tmp_path):
+    """Each rank computes only its heads (no collective in the path); the
+    concatenated shards equal the unsharded result exactly."""
+    import socket
+
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    res = tmp_path / "res.txt"
+    mp.start_processes(_sharded_worker, args=(2, port, str(res)), nprocs=2, join=True,
+                       start_method="spawn")
+    assert res.read_text() == "ok"
+
+
+# -------------------------------------------------- indexer host chunking
+def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch):
+    """The host loop (workspace chunks, decode/prefill split, visible blocks)
+    driven with the oracle standing in for the two kernels must reproduce the
+    oracle's one-shot result."""
+    import qsa_vllm_b200.indexer as I
+
+    def fake_scores(q, k_cache, page_table, visible, logits, *, decode_query_len=1,
+                    query_start_loc=None, max_query_len=0, query_offset=0, num_rows=None,
+                    weights=None, scale=None):
+        rows = q.shape[0] if num_rows is None else num_rows
+        if query_start_loc is None:
+            res = O.indexer_scores(q, k_cache, page_table, visible, logits.shape[1],
+                                   decode_query_len=decode_query_len, weights=weights,
+                                   scale=scale)
+            logits.copy_(torch.nan_to_num(res, nan=0.0))
+        else:
+            res = O.indexer_scores(q, k_cache, page_table, visible, logits.shape[1],
+                                   query_start_loc=query_start_loc, weights=weights, scale=scale)
+            logits.copy_(torch.nan_to_num(res[query_offset:query_offset + rows], nan=0.0))
+
+    def fake_topk(scores, lengths, positions, seq_lens, t2r, output, ratio, *,
+                  main_block_table=None, main_page_size=1, valid_counts_out=None):
+        out, counts = O.topk_expand(scores, lengths, positions, seq_lens, t2r, main_block_table,
+                                    output.shape[1], ratio, page_size=main_page_size)
+        output.copy_(torch.from_numpy(out))
+        if valid_counts_out is not None:
+            valid_counts_out.copy_(torch.from_numpy(counts))
+
+    monkeypatch.setattr(I, "indexer_scores", fake_scores)
+    monkeypatch.setattr(I, "_topk_expand", fake_topk)
+    monkeypatch.setattr(I, "_INDEXER_WORKSPACE_BYTES", 3 * 64 * 4)   # force many chunks
+    g = torch.Generator().manual_seed(0)
+    ratio, page, topk = 4, 16, 32
+    seq = torch.tensor([300, 180, 260], dtype=torch.int32)
+    # 2 decode requests then one prefill request of 5 tokens
+    t2r = torch.tensor([0, 1, 2, 2, 2, 2, 2], dtype=torch.int32)
+    pos = torch.tensor([299, 179, 255, 256, 257, 258, 259], dtype=torch.int64)
+    qsl = torch.tensor([0, 1, 2, 7], dtype=torch.int32)
+    nblk = 30
+    kc = torch.randn(nblk, page, 1, 64, generator=g).to(torch.bfloat16)
+    table = torch.randperm(nblk, generator=g)[:15].view(3, 5).to(torch.int32)
+    q = torch.randn(7, 4, 64, generator=g).to(torch.bfloat16)
+    out = torch.empty(7, topk + ratio - 1, dtype=torch.int32)
+    I.select_paged_tokens(q, kc, table, t2r, pos, seq, topk, ratio, out, query_start_loc=qsl,
+                          max_query_len=5, max_seq_len=300, num_decodes=2, num_decode_tokens=2)
+    vis = O.visible_blocks(pos, seq, t2r, ratio)
+    logits = torch.zeros(7, 80)
+    for r in range(7):
+        req = int(t2r[r])
+        logits[r] = torch.nan_to_num(O.indexer_scores(q[r:r + 1], kc, table[req:req + 1],
+                                                      vis[r:r + 1], 80), nan=0.0)[0]
+    ref, _ = O.topk_expand(logits, vis, pos, seq, t2r, None, topk + ratio - 1, ratio)
+    assert np.array_equal(out.numpy(), ref)
