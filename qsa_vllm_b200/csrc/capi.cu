@@ -199,7 +199,9 @@ int qsa_topk_expand(const float* scores, int64_t score_row_stride, int32_t rows,
   p.counts = counts;
   p.ratio = ratio;
   p.page_size = physical ? page_size : 1;
+  p.page_div = FastDiv(static_cast<uint32_t>(p.page_size));
   p.physical = physical ? 1 : 0;
+  p.aligned_blocks = (physical && page_size % ratio == 0) ? 1 : 0;
   p.expand = 1;
   p.topk = output_width / ratio;
   return topk_common(p, stream, "qsa_topk_expand");
@@ -275,6 +277,7 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
   p.token_stride = cache_token_stride;
   p.num_blocks = num_blocks;
   p.page_size = page_size;
+  p.page_div = FastDiv(static_cast<uint32_t>(page_size));
   p.table = page_table;
   p.table_row_stride = table_row_stride;
   p.table_width = table_width;
@@ -342,9 +345,10 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
       k_token_stride % 8 || k_head_stride % 8 || v_block_stride % 8 || v_token_stride % 8 ||
       v_head_stride % 8)
     return fail(QSA_ERR_INVALID, "%s: K/V cache rows must be 16-byte aligned", who);
-  if (!aligned(q, 4) || q_row_stride % 2 || q_head_stride % 2 || !aligned(out, 4) ||
-      out_row_stride % 2 || out_head_stride % 2)
-    return fail(QSA_ERR_INVALID, "%s: q / out rows must be 4-byte aligned", who);
+  if (!aligned(q, 16) || q_row_stride % 8 || q_head_stride % 8)
+    return fail(QSA_ERR_INVALID, "%s: q head rows must be 16-byte aligned", who);
+  if (!aligned(out, 4) || out_row_stride % 2 || out_head_stride % 2)
+    return fail(QSA_ERR_INVALID, "%s: out rows must be 4-byte aligned", who);
   const AttnPlan plan =
       plan_attention(rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel);
   if (plan.workspace_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.workspace_bytes))
@@ -369,6 +373,7 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.v_head_stride = v_head_stride;
   p.num_blocks = num_blocks;
   p.page_size = page_size;
+  p.page_div = FastDiv(static_cast<uint32_t>(page_size));
   p.kv_heads = num_kv_heads;
   p.indices = indices;
   p.indices_row_stride = indices_row_stride;
@@ -389,10 +394,13 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.scale_log2 = static_cast<float>(std::pow(static_cast<double>(head_dim), -0.5) *
                                     1.4426950408889634);
   p.physical = indices_are_physical ? 1 : 0;
-  p.kv_fused = (static_cast<const char*>(v_cache) ==
-                static_cast<const char*>(k_cache) + 2 * head_dim) &&
-               k_block_stride == v_block_stride && k_token_stride == v_token_stride &&
-               k_head_stride == v_head_stride;
+  // 2: each token's K||V rows of consecutive KV heads form one run (the
+  //    [blocks, page, H_kv, K||V] layout); 1: K||V adjacent per head; 0: apart.
+  const bool fused = (static_cast<const char*>(v_cache) ==
+                      static_cast<const char*>(k_cache) + 2 * head_dim) &&
+                     k_block_stride == v_block_stride && k_token_stride == v_token_stride &&
+                     k_head_stride == v_head_stride;
+  p.kv_fused = fused ? (k_head_stride == 2 * head_dim ? 2 : 1) : 0;
   p.splits = plan.splits;
   if (plan.splits > 1) {
     const size_t o_bytes =

@@ -142,4 +142,30 @@ __device__ __forceinline__ void record_error(int* err, int bits) {
   if (err != nullptr) atomicOr(err, bits);
 }
 
+// Division of non-negative 32-bit integers by a run-time constant through a
+// multiply-high (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, unsigned case): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1,  n / d = (t + ((n - t) >> min(l,1))) >> max(l-1,0)
+// where t = umulhi(m, n).  Exact for all n < 2^32, 1 <= d < 2^31.
+struct FastDiv {
+  uint32_t d, m, s1, s2;
+  __host__ __device__ FastDiv() : d(1), m(1), s1(0), s2(0) {}
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    uint32_t l = 0;
+    while ((1ull << l) < divisor) ++l;
+    m = static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - divisor)) / divisor + 1);
+    s1 = l < 1 ? l : 1;
+    s2 = l > 0 ? l - 1 : 0;
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    const uint32_t t = __umulhi(m, n);
+    return (t + ((n - t) >> s1)) >> s2;
+  }
+  // quotient and remainder of a non-negative int
+  __device__ __forceinline__ void divmod(int n, int& q, int& r) const {
+    q = static_cast<int>(div(static_cast<uint32_t>(n)));
+    r = n - q * static_cast<int>(d);
+  }
+};
+
 }  // namespace qsa

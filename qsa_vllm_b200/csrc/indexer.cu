@@ -25,6 +25,8 @@ namespace {
 constexpr int kKeyTile = 64;
 constexpr int kStages = 4;
 constexpr int kThreads = 128;
+constexpr int kMaxKeysPerCta = 1024;
+constexpr int kMaxPages = kMaxKeysPerCta + 2;  // page size 1 worst case
 
 template <int D, int NT>
 struct IdxSmem {
@@ -33,6 +35,7 @@ struct IdxSmem {
   alignas(128) uint8_t q[8 * NT * kRowBytes];
   float w[8 * NT];
   int limit[8 * NT];  // per row of the CTA: columns below this are stored
+  int pages[kMaxPages];  // physical page of each logical page of this CTA's keys
 };
 
 // byte offset of 16-byte chunk `c` of row `r` in a swizzled tile
@@ -96,7 +99,13 @@ __global__ void __launch_bounds__(kThreads) indexer_kernel(const IndexerParams p
     cp_async16(sm.q + swz<D>(n, c), src, v);
   }
 
+  // ---- this CTA's slice of the page table, staged once in shared memory so
+  // the key-tile loads below never wait on a dependent global lookup.
   const int32_t* trow = p.table + static_cast<int64_t>(req) * p.table_row_stride;
+  const int pg0 = static_cast<int>(p.page_div.div(k0));
+  const int npg = static_cast<int>(p.page_div.div(k1 - 1)) - pg0 + 1;
+  for (int i = tid; i < npg; i += kThreads) sm.pages[i] = trow[pg0 + i];
+  __syncthreads();
   const __nv_bfloat16* kb = static_cast<const __nv_bfloat16*>(p.k_cache);
   const int ntiles = (k1 - k0 + kKeyTile - 1) / kKeyTile;
   auto load_tile = [&](int t) {
@@ -105,14 +114,15 @@ __global__ void __launch_bounds__(kThreads) indexer_kernel(const IndexerParams p
       const int key = ch / CPR, c = ch % CPR;
       const int col = k0 + t * kKeyTile + key;
       bool v = col < k1;
-      int page = 0;
+      int page = 0, lp = 0, off = 0;
       if (v) {
-        page = trow[col / p.page_size];
+        p.page_div.divmod(col, lp, off);
+        page = sm.pages[lp - pg0];
         v = page >= 0 && page < p.num_blocks;
       }
       const __nv_bfloat16* src =
           kb + (v ? static_cast<int64_t>(page) * p.block_stride +
-                        static_cast<int64_t>(col % p.page_size) * p.token_stride
+                        static_cast<int64_t>(off) * p.token_stride
                   : 0) +
           c * 8;
       cp_async16(dst + swz<D>(key, c), src, v);
@@ -253,7 +263,7 @@ cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
     rows_per_cta = p.decode_query_len;
     requests = p.num_rows / p.decode_query_len;
     row_tiles = 1;
-    keys_per_cta = 1024;
+    keys_per_cta = kMaxKeysPerCta;
   } else {
     rows_per_cta = std::max(1, 128 / H);
     requests = p.num_requests;

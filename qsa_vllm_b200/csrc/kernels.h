@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace qsa {
 
 // ----------------------------------------------------------------- top-k
@@ -26,7 +28,9 @@ struct TopkParams {
   int out_width;
   int32_t* counts;
   int ratio, page_size;
+  FastDiv page_div;  // division by page_size
   int physical;   // expansion maps tokens to slots through `table`
+  int aligned_blocks;  // physical && page_size % ratio == 0: one lookup per block
   int expand;     // 0: plain ids (torch.ops...topk), 1: expanded tokens
   int topk;       // selected blocks per row
   int slice_cap;  // keys held in shared memory per CTA
@@ -45,6 +49,7 @@ struct IndexerParams {
   const void* k_cache;
   int64_t block_stride, token_stride;
   int num_blocks, page_size;
+  FastDiv page_div;  // division by page_size
   const int32_t* table;
   int64_t table_row_stride;
   int table_width, num_requests;
@@ -71,6 +76,7 @@ struct AttnParams {
   const void* v_cache;
   int64_t v_block_stride, v_token_stride, v_head_stride;
   int num_blocks, page_size, kv_heads;
+  FastDiv page_div;  // division by page_size
   const int32_t* indices;
   int64_t indices_row_stride;
   int topk_width;
@@ -85,7 +91,7 @@ struct AttnParams {
   int64_t out_row_stride, out_head_stride;
   float scale_log2;  // head_dim^-0.5 * log2(e), rounded once to fp32 (ops/qsa.py:176)
   int physical;
-  int kv_fused;     // V row directly follows the K row: one copy per token
+  int kv_fused;     // 2: K||V of consecutive heads contiguous; 1: per head; 0: apart
   int splits;       // split-K factor per (row, kv head)
   float* part_o;    // [splits, rows, q_heads, dim] fp32 (splits > 1)
   float* part_lse;  // [splits, rows, q_heads] fp32

@@ -6,19 +6,23 @@
 // column, and the selection is emitted in ascending column order; rows whose
 // length is <= K emit 0..length-1.
 //
-// Design (B200): one thread-block CLUSTER per row.  Each CTA of the cluster
-// loads its contiguous slice of the row ONCE from HBM into shared memory
-// (16-byte loads), and every later pass runs out of shared memory:
-//   * radix select, most-significant digit first, 11/11/10-bit digits; the
-//     per-CTA histograms are summed across the cluster through distributed
-//     shared memory (DSMEM), so every CTA derives the same threshold;
-//   * a pass stops early once the threshold digit's bucket is taken whole;
-//   * the ordered write-out is a block scan of (strictly-above, tied) flags per
-//     CTA plus an exchange of per-CTA totals over DSMEM: tied keys are taken
-//     in ascending column order across the cluster, exactly as the reference.
-// No global scratch memory is used: a row is selected in one launch whatever
-// its width (the reference needs a partition + merge pass above 32768 columns).
+// Design (B200), latency first (a decode step selects over only ~2-8 MB):
+//   * one CTA of 512 threads per row slice; each thread keeps its keys (16,
+//     or 64 for very wide rows) in REGISTERS after one coalesced 16-byte load
+//     pass from HBM, so every radix pass re-reads registers, not memory;
+//   * radix select, most-significant digit first, 11/11/10-bit digits, with
+//     warp-aggregated shared-memory histograms (double-buffered, so a pass
+//     needs a single barrier); a pass stops early once the threshold digit's
+//     bucket is taken whole;
+//   * rows wider than one CTA's slice run as a thread-block CLUSTER: the
+//     per-CTA histograms are summed through distributed shared memory (DSMEM)
+//     and every CTA derives the same threshold; tied keys are then taken in
+//     ascending column order across the cluster from per-CTA totals;
+//   * no global scratch memory: one launch whatever the width (the reference
+//     needs a partition + merge pass above 32768 columns).
 #include <cooperative_groups.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -28,10 +32,9 @@ namespace cg = cooperative_groups;
 namespace qsa {
 namespace {
 
-constexpr int kThreads = 1024;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 2048;
-constexpr int kMaxSliceBytes = 160 * 1024;
 constexpr int kMaxCluster = 16;
 
 struct RowMeta {
@@ -59,24 +62,53 @@ __device__ __forceinline__ RowMeta row_meta(const TopkParams& p, int row) {
 __device__ __forceinline__ int map_token(const TopkParams& p, const RowMeta& m, int token) {
   if (token < 0 || token >= m.seq) return -1;
   if (!p.physical) return token;
-  const int lp = token / p.page_size;
+  int lp, off;
+  p.page_div.divmod(token, lp, off);
   if (lp >= p.table_width) return -1;
-  const int ph = m.trow[lp];
-  return ph >= 0 ? ph * p.page_size + token % p.page_size : -1;
+  const int ph = __ldg(m.trow + lp);
+  return ph >= 0 ? ph * p.page_size + off : -1;
+}
+
+// Physical page of a selected block's first token, for the expansion fast
+// path (page_size % ratio == 0: the block's tokens share one page).  -1 when
+// unmapped or past the sequence.
+__device__ __forceinline__ int block_page(const TopkParams& p, const RowMeta& m, int first) {
+  if (first < 0 || first >= m.seq) return -1;
+  int lp, off;
+  p.page_div.divmod(first, lp, off);
+  return lp < p.table_width ? __ldg(m.trow + lp) : -1;
+}
+
+// Writes the expansion of `block` at rank `rank` (block -1 writes -1s).
+// `ph` is block_page() when p.aligned_blocks (ignored otherwise).
+__device__ __forceinline__ void store_block(const TopkParams& p, const RowMeta& m,
+                                            int32_t* out_row, int rank, int block, int ph) {
+  if (!p.expand) {
+    out_row[rank] = block;
+    return;
+  }
+  const int first = block * p.ratio;
+  int32_t* dst = out_row + static_cast<int64_t>(rank) * p.ratio * p.out_col_stride;
+  if (p.aligned_blocks) {
+    int lp = 0, off = 0;
+    if (ph >= 0) p.page_div.divmod(first, lp, off);
+    for (int o = 0; o < p.ratio; ++o) {
+      const int token = first + o;
+      dst[static_cast<int64_t>(o) * p.out_col_stride] =
+          (ph >= 0 && token < m.seq) ? ph * p.page_size + off + o : -1;
+    }
+  } else {
+    for (int o = 0; o < p.ratio; ++o)
+      dst[static_cast<int64_t>(o) * p.out_col_stride] = map_token(p, m, first + o);
+  }
 }
 
 // Writes the selection of rank `rank` (block id or -1).
 __device__ __forceinline__ void write_rank(const TopkParams& p, const RowMeta& m,
                                            int32_t* out_row, int rank, int block) {
-  if (!p.expand) {
-    out_row[rank] = block;
-    return;
-  }
-  if (rank >= m.complete) return;
-  const int first = block * p.ratio;
-  for (int o = 0; o < p.ratio; ++o)
-    out_row[static_cast<int64_t>(rank * p.ratio + o) * p.out_col_stride] =
-        map_token(p, m, first + o);
+  if (p.expand && rank >= m.complete) return;
+  const int ph = (p.expand && p.aligned_blocks) ? block_page(p, m, block * p.ratio) : 0;
+  store_block(p, m, out_row, rank, block, ph);
 }
 
 // Causal tail, -1 fill and valid count (topk.cu:152-162).
@@ -95,6 +127,7 @@ __device__ __forceinline__ void finish_row(const TopkParams& p, const RowMeta& m
 
 // Warp-aggregated shared-memory histogram increment (all 32 lanes call it).
 __device__ __forceinline__ void hist_add(int* hist, bool valid, uint32_t bin) {
+  if (!__any_sync(0xffffffffu, valid)) return;
   const uint32_t key = valid ? bin : 0xffffffffu;
   const unsigned peers = __match_any_sync(0xffffffffu, key);
   if (valid && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
@@ -113,13 +146,13 @@ __device__ __forceinline__ int block_exclusive_sum(int v, int* warp_tmp, int& to
   if (lane == 31) warp_tmp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = warp_tmp[lane];
+    int w = lane < kWarps ? warp_tmp[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    warp_tmp[lane] = w;  // inclusive warp prefix
+    if (lane < kWarps) warp_tmp[lane] = w;  // inclusive warp prefix
   }
   __syncthreads();
   total = warp_tmp[kWarps - 1];
@@ -129,8 +162,12 @@ __device__ __forceinline__ int block_exclusive_sum(int v, int* warp_tmp, int& to
   return result;
 }
 
+// V keys per thread; the slice of a CTA is kThreads * V keys, stored as
+// V/4 chunks of kThreads float4 (thread t holds keys 4*(c*kThreads+t)+0..3).
+template <int V>
 __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
-  extern __shared__ __align__(16) uint32_t keys[];
+  constexpr int kChunks = V / 4;
+  constexpr int kChunkKeys = 4 * kThreads;
   __shared__ int hist[2][kBins];
   __shared__ int warp_tmp[kWarps];
   __shared__ int s_bin, s_remaining, s_bin_count;
@@ -156,172 +193,169 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     return;  // uniform across the cluster: no CTA reaches a cluster barrier
   }
 
-  // ---- slice of this CTA, loaded once; pass-0 histogram fused with the load.
+  // ---- this CTA's slice -> registers (one pass over HBM).
   const int per = ((length + C - 1) / C + 3) & ~3;
   const int begin = min(crank * per, length);
   const int n = min(begin + per, length) - begin;
   for (int b = tid; b < 2 * kBins; b += kThreads) (&hist[0][0])[b] = 0;
-  __syncthreads();
   const float* src = p.scores + static_cast<int64_t>(row) * p.score_row_stride + begin;
-  if (p.vec4) {
-    const int n4 = (n + 3) >> 2;
-    for (int base = 0; base < n4; base += kThreads) {
-      const int i = base + tid;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      const int e = i * 4;
-      if (e + 3 < n) {
-        v = __ldg(reinterpret_cast<const uint4*>(src) + i);
-      } else if (e < n) {
-        v.x = __float_as_uint(src[e]);
-        if (e + 1 < n) v.y = __float_as_uint(src[e + 1]);
-        if (e + 2 < n) v.z = __float_as_uint(src[e + 2]);
-      }
-      if (i < n4) reinterpret_cast<uint4*>(keys)[i] = v;
-      hist_add(hist[0], e < n, v.x >> 21);
-      hist_add(hist[0], e + 1 < n, v.y >> 21);
-      hist_add(hist[0], e + 2 < n, v.z >> 21);
-      hist_add(hist[0], e + 3 < n, v.w >> 21);
-    }
-  } else {
-    for (int base = 0; base < n; base += kThreads) {
-      const int i = base + tid;
-      const uint32_t k = i < n ? __float_as_uint(src[i]) : 0u;
-      if (i < n) keys[i] = k;
-      hist_add(hist[0], i < n, k >> 21);
+  uint32_t key[V];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int e = 4 * (c * kThreads + tid);
+    if (p.vec4 && e + 3 < n) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + e));
+      key[4 * c] = v.x;
+      key[4 * c + 1] = v.y;
+      key[4 * c + 2] = v.z;
+      key[4 * c + 3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) key[4 * c + j] = e + j < n ? __float_as_uint(src[e + j]) : 0u;
     }
   }
+  auto valid_at = [&](int i) { return 4 * ((i / 4) * kThreads + tid) + (i % 4) < n; };
+  const int chunks_used = (n + kChunkKeys - 1) / kChunkKeys;
   __syncthreads();
+#pragma unroll
+  for (int i = 0; i < V; ++i) hist_add(hist[0], valid_at(i), key[i] >> 21);
 
   // ---- radix passes: digits of 11, 11, 10 bits from the most significant.
-  uint32_t prefix = 0;  // resolved high bits: selection threshold is (key >> shift) == prefix
+  uint32_t prefix = 0;  // resolved high bits: the threshold is (key >> shift) == prefix
   int shift = 32;
   int remaining = topk;  // how many of the keys matching `prefix` are still to be taken
-  int buf = 0;
   for (int pass = 0;; ++pass) {
+    const int b = pass & 1;
     const int dbits = pass < 2 ? 11 : 10;
     const int dshift = shift - dbits;
     const uint32_t dmask = (1u << dbits) - 1u;
     if (pass > 0) {
-      for (int b = tid; b < kBins; b += kThreads) hist[buf][b] = 0;
-      __syncthreads();
-      const int n4 = (n + 3) >> 2;
-      for (int base = 0; base < n4; base += kThreads) {
-        const int i = base + tid;
-        const uint4 v = i < n4 ? reinterpret_cast<const uint4*>(keys)[i] : make_uint4(0, 0, 0, 0);
-        const int e = i * 4;
-        hist_add(hist[buf], e < n && (v.x >> shift) == prefix, (v.x >> dshift) & dmask);
-        hist_add(hist[buf], e + 1 < n && (v.y >> shift) == prefix, (v.y >> dshift) & dmask);
-        hist_add(hist[buf], e + 2 < n && (v.z >> shift) == prefix, (v.z >> dshift) & dmask);
-        hist_add(hist[buf], e + 3 < n && (v.w >> shift) == prefix, (v.w >> dshift) & dmask);
+      if (pass >= 2) {  // hist[b] was last read by the cluster two passes ago
+        for (int i = tid; i < kBins; i += kThreads) hist[b][i] = 0;
+        __syncthreads();
       }
-      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < V; ++i)
+        hist_add(hist[b], valid_at(i) && (key[i] >> shift) == prefix, (key[i] >> dshift) & dmask);
     }
-    cluster.sync();  // every CTA's histogram of this pass is complete
+    __syncthreads();
+    if (C > 1) cluster.sync();  // every CTA's histogram of this pass is complete
 
-    // Thread t owns the two bins just below the 2t highest (descending order).
+    // Thread t owns the 4 bins just below the 4t highest (descending order).
     const int nb = 1 << dbits;
-    const int per_thread = nb / kThreads;  // 2 or 1
-    const int b_hi = nb - 1 - per_thread * tid;
-    const int b_lo = b_hi - 1;
-    int h_hi = 0, h_lo = 0;
-    for (int r = 0; r < C; ++r) {
-      const int* rh = cluster.map_shared_rank(&hist[buf][0], r);
-      h_hi += rh[b_hi];
-      if (per_thread == 2) h_lo += rh[b_lo];
+    const int per_thread = nb / kThreads;  // 4 or 2
+    const int top = nb - 1 - per_thread * tid;
+    int h[4] = {0, 0, 0, 0};
+    if (C > 1) {
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r) {
+        if (r < C) {
+          const int* rh = cluster.map_shared_rank(&hist[b][0], r);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < per_thread) h[j] += rh[top - j];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < per_thread) h[j] = hist[b][top - j];
     }
     int total;
-    const int above = block_exclusive_sum(h_hi + h_lo, warp_tmp, total);
-    if (above < remaining && remaining <= above + h_hi) {
-      s_bin = b_hi;
-      s_remaining = remaining - above;
-      s_bin_count = h_hi;
-    } else if (per_thread == 2 && above + h_hi < remaining && remaining <= above + h_hi + h_lo) {
-      s_bin = b_lo;
-      s_remaining = remaining - above - h_hi;
-      s_bin_count = h_lo;
+    int above = block_exclusive_sum(h[0] + h[1] + h[2] + h[3], warp_tmp, total);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j < per_thread && above < remaining && remaining <= above + h[j]) {
+        s_bin = top - j;
+        s_remaining = remaining - above;
+        s_bin_count = h[j];
+      }
+      above += h[j];
     }
     __syncthreads();
     prefix = (prefix << dbits) | static_cast<uint32_t>(s_bin);
     remaining = s_remaining;
     shift = dshift;
     const bool done = s_bin_count == remaining || shift == 0;
-    buf ^= 1;
-    __syncthreads();
+    __syncthreads();  // s_* are rewritten by the next pass
     if (done) break;
   }
 
   // ---- ordered write-out.  strict: (key >> shift) > prefix; tie: == prefix.
   int my_strict = 0, my_tie = 0;
-  const int n4 = (n + 3) >> 2;
-  for (int i = tid; i < n4; i += kThreads) {
-    const uint4 v = reinterpret_cast<const uint4*>(keys)[i];
-    const uint32_t kk[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (i * 4 + j < n) {
-        const uint32_t d = kk[j] >> shift;
-        my_strict += d > prefix;
-        my_tie += d == prefix;
-      }
-    }
+  for (int i = 0; i < V; ++i) {
+    const uint32_t d = key[i] >> shift;
+    my_strict += valid_at(i) && d > prefix;
+    my_tie += valid_at(i) && d == prefix;
   }
-  int tot_strict, tot_tie;
+  int tot_strict, tot_tie;  // up to 32768 each: two sums, no 16-bit packing
   block_exclusive_sum(my_strict, warp_tmp, tot_strict);
   block_exclusive_sum(my_tie, warp_tmp, tot_tie);
-  if (tid == 0) {
-    s_counts[0] = tot_strict;
-    s_counts[1] = tot_tie;
-  }
-  cluster.sync();  // per-CTA totals visible cluster-wide
   int base_rank = 0, ties_before = 0;
-  for (int r = 0; r < crank; ++r) {
-    const int* rc = cluster.map_shared_rank(&s_counts[0], r);
-    const int quota_r = min(max(remaining - ties_before, 0), rc[1]);
-    base_rank += rc[0] + quota_r;
-    ties_before += rc[1];
+  if (C > 1) {
+    if (tid == 0) {
+      s_counts[0] = tot_strict;
+      s_counts[1] = tot_tie;
+    }
+    cluster.sync();  // per-CTA totals visible cluster-wide
+    for (int r = 0; r < crank; ++r) {
+      const int* rc = cluster.map_shared_rank(&s_counts[0], r);
+      const int quota_r = min(max(remaining - ties_before, 0), rc[1]);
+      base_rank += rc[0] + quota_r;
+      ties_before += rc[1];
+    }
   }
   const int quota = min(max(remaining - ties_before, 0), tot_tie);
 
   int run_strict = 0, run_tie = 0;
-  for (int base = 0; base < n4; base += kThreads) {
-    const int i = base + tid;
-    const uint4 v = i < n4 ? reinterpret_cast<const uint4*>(keys)[i] : make_uint4(0, 0, 0, 0);
-    const uint32_t kk[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    if (c >= chunks_used) break;  // uniform across the CTA
     int fs = 0, ft = 0;
-    uint32_t flags = 0;  // bit 2j: strict, bit 2j+1: tie
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (i < n4 && i * 4 + j < n) {
-        const uint32_t d = kk[j] >> shift;
-        if (d > prefix) {
-          flags |= 1u << (2 * j);
-          ++fs;
-        } else if (d == prefix) {
-          flags |= 2u << (2 * j);
-          ++ft;
-        }
-      }
+      const uint32_t d = key[4 * c + j] >> shift;
+      const bool v = valid_at(4 * c + j);
+      fs += v && d > prefix;
+      ft += v && d == prefix;
     }
     int round_total;
     const int ex = block_exclusive_sum((fs << 16) | ft, warp_tmp, round_total);
     int sb = run_strict + (ex >> 16);
     int tb = run_tie + (ex & 0xffff);
+    int rank[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int id = begin + i * 4 + j;
-      if (flags & (1u << (2 * j))) {
-        write_rank(p, m, out_row, base_rank + sb + min(tb, quota), id);
+      const uint32_t d = key[4 * c + j] >> shift;
+      const bool v = valid_at(4 * c + j);
+      rank[j] = -1;
+      if (v && d > prefix) {
+        rank[j] = base_rank + sb + min(tb, quota);
         ++sb;
-      } else if (flags & (2u << (2 * j))) {
-        if (tb < quota) write_rank(p, m, out_row, base_rank + sb + tb, id);
+      } else if (v && d == prefix) {
+        if (tb < quota) rank[j] = base_rank + sb + tb;
         ++tb;
       }
+      if (p.expand && rank[j] >= m.complete) rank[j] = -1;
     }
+    // page lookups of this thread's selected blocks first (independent loads),
+    // then the stores
+    int ph[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int id = begin + 4 * (c * kThreads + tid) + j;
+      ph[j] = (rank[j] >= 0 && p.expand && p.aligned_blocks) ? block_page(p, m, id * p.ratio) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (rank[j] >= 0)
+        store_block(p, m, out_row, rank[j], begin + 4 * (c * kThreads + tid) + j, ph[j]);
     run_strict += round_total >> 16;
     run_tie += round_total & 0xffff;
   }
   if (crank == 0 && p.expand) finish_row(p, m, out_row, row);
-  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
+  if (C > 1) cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
 int pow2_ceil(int x) {
@@ -330,35 +364,17 @@ int pow2_ceil(int x) {
   return c;
 }
 
-}  // namespace
-
-int topk_max_width() { return kMaxCluster * (kMaxSliceBytes / 4); }
-
-cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_cluster) {
-  TopkParams p = p0;
-  if (p.rows <= 0) return cudaSuccess;
-  const int sms = num_sms();
-  int C = pow2_ceil((2 * sms + p.rows - 1) / p.rows);
-  C = std::min(C, 8);
-  int by_width = 1;
-  while (by_width * 2 * 1024 <= p.width) by_width *= 2;
-  C = std::max(1, std::min(C, by_width));
-  auto cap_of = [&](int c) { return (((p.width + c - 1) / c) + 3) & ~3; };
-  while (cap_of(C) * 4 > kMaxSliceBytes && C < kMaxCluster) C *= 2;
-  if (cap_of(C) * 4 > kMaxSliceBytes) return cudaErrorInvalidValue;
-  p.slice_cap = cap_of(C);
-  const size_t smem = static_cast<size_t>(p.slice_cap) * 4;
-  cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kMaxSliceBytes);
-  if (e != cudaSuccess) return e;
+template <int V>
+cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
   if (C > 8) {
-    e = set_attr_once(reinterpret_cast<const void*>(topk_kernel), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_kernel<V>),
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -367,8 +383,28 @@ cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_clu
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, topk_kernel<V>, p);
+}
+
+}  // namespace
+
+int topk_max_width() { return kMaxCluster * kThreads * 64; }
+
+cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_cluster) {
+  TopkParams p = p0;
+  if (p.rows <= 0) return cudaSuccess;
+  // Smallest (keys per thread, cluster width) whose slices cover the row.
+  const int w = std::max(p.width, 1);
+  int V = 16;
+  int C = pow2_ceil((w + kThreads * V - 1) / (kThreads * V));
+  if (C > kMaxCluster) {
+    V = 64;
+    C = pow2_ceil((w + kThreads * V - 1) / (kThreads * V));
+  }
+  if (C > kMaxCluster) return cudaErrorInvalidValue;
+  p.slice_cap = kThreads * V;
   if (plan_cluster) *plan_cluster = C;
-  return cudaLaunchKernelEx(&cfg, topk_kernel, p);
+  return V == 16 ? launch_v<16>(p, C, stream) : launch_v<64>(p, C, stream);
 }
 
 }  // namespace qsa

@@ -1,0 +1,114 @@
+"""Run one stage of the QSA path in a loop, for profilers (ncu) and quick timing.
+
+    python -m qsa_vllm_b200.profile_kernels --kernel attention --config cfg2_32k \
+        --batch 16 --iters 3 [--contiguous-tables] [--time]
+
+``--kernel``: ``indexer`` | ``topk`` | ``attention`` | ``step`` (all three).
+Inputs are the synthetic workload of ``--config`` with ``--batch`` rows (the
+same per-row shapes as the benchmark, a smaller device footprint for ncu
+captures).  ``--contiguous-tables`` replaces the random block tables with the
+identity layout (each request's pages consecutive in memory), which isolates
+the cost of scattered pages.  ``--time`` prints CUDA-event timings with the L2
+flushed before every iteration.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from .indexer import indexer_scores, select_paged_tokens
+from .qsa import qsa_sparse_paged_attention
+from .synthetic import make_workload
+from .topk import topk_expand
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="attention",
+                    choices=["indexer", "topk", "attention", "step"])
+    ap.add_argument("--config", default="cfg2_32k")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--contiguous-tables", action="store_true")
+    ap.add_argument("--time", action="store_true")
+    a = ap.parse_args()
+    dev = torch.device("cuda")
+    w = make_workload(a.config, device=dev, seed=0, batch=a.batch)
+    if a.contiguous_tables:
+        for name in ("block_table", "index_table"):
+            t = getattr(w, name)
+            pages = (t >= 0).sum(1)
+            start = torch.cumsum(pages, 0) - pages
+            ident = start[:, None] + torch.arange(t.shape[1], device=dev)[None, :]
+            setattr(w, name, torch.where(t >= 0, ident, t).to(torch.int32))
+    rows = w.rows
+    width = w.token_topk + w.ratio - 1
+    r = w.ratio
+    vis = torch.minimum((w.positions + 1) // r, w.seq_lens.long()[w.token_to_req.long()] // r)
+    vis = vis.to(torch.int32)
+    cols = w.index_table.shape[1] * w.index_cache.shape[1]
+    logits = torch.zeros(rows, cols, device=dev)
+    idx = torch.empty(rows, width, dtype=torch.int32, device=dev)
+    cnt = torch.empty(rows, dtype=torch.int32, device=dev)
+    out = torch.empty_like(w.q)
+
+    def run_indexer():
+        indexer_scores(w.index_q, w.index_cache, w.index_table, vis, logits,
+                       weights=w.index_weights, scale=w.index_scale)
+
+    def run_topk():
+        topk_expand(logits, vis, w.positions, w.seq_lens, w.token_to_req, idx, r,
+                    main_block_table=w.block_table, main_page_size=w.page_size,
+                    valid_counts_out=cnt)
+
+    def run_attention():
+        qsa_sparse_paged_attention(w.q, w.k_cache, w.v_cache, idx, w.block_table, w.token_to_req,
+                                   out, output_gate=w.gate, use_decode_kernel=True,
+                                   indices_are_physical=True, valid_counts=cnt)
+
+    def run_step():
+        select_paged_tokens(
+            w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
+            w.token_topk, r, idx, query_start_loc=w.query_start_loc, max_query_len=1,
+            max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt,
+            weights=w.index_weights, scale=w.index_scale)
+        run_attention()
+
+    run_indexer()
+    run_topk()
+    fn = {"indexer": run_indexer, "topk": run_topk, "attention": run_attention,
+          "step": run_step}[a.kernel]
+    for _ in range(a.warmup):
+        fn()
+    torch.cuda.synchronize()
+    if not a.time:
+        for _ in range(a.iters):
+            fn()
+        torch.cuda.synchronize()
+        return
+    graph = torch.cuda.CUDAGraph()   # replay: no host launch gaps inside the events
+    with torch.cuda.graph(graph):
+        fn()
+    graph.replay()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(a.iters)]
+    for s, e in ev:
+        flush.zero_()
+        s.record()
+        graph.replay()
+        e.record()
+    torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in ev]
+    print(json.dumps({"kernel": a.kernel, "config": a.config, "rows": rows,
+                      "contiguous_tables": a.contiguous_tables, "ms_min": min(ms),
+                      "ms_median": sorted(ms)[len(ms) // 2]}))
+
+
+if __name__ == "__main__":
+    main()

@@ -60,6 +60,8 @@ def qsa_sparse_paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: 
     gate = output_gate
     if gate is not None and gate.dtype != torch.bfloat16:
         raise TypeError("output_gate must be bfloat16")
+    if q.data_ptr() % 16 or q.stride(0) % 8 or q.stride(1) % 8:
+        q = q.contiguous()   # query rows are bulk-copied: 16-byte aligned head rows
     hq, d = q.shape[1], q.shape[2]
     hkv = k_cache.shape[2]
     width = logical_indices.shape[1]

@@ -76,12 +76,12 @@ class SyntheticQSA:
 
     @property
     def max_seq_len(self) -> int:
-        return int(self.seq_lens.max())
+        """Host-side value (no device sync: safe inside CUDA-graph capture)."""
+        return self.extra["max_seq_len"]
 
     @property
     def max_query_len(self) -> int:
-        q = self.query_start_loc
-        return int((q[1:] - q[:-1]).max())
+        return self.extra["max_query_len"]
 
     def shard_heads(self, tp_size: int, tp_rank: int) -> "SyntheticQSA":
         """This rank's view under head (tensor-parallel) sharding: query heads and
@@ -116,8 +116,7 @@ def _tables(gen: torch.Generator, pages_per_req: list[int], device) -> tuple[tor
 
 def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
                   batch: int | None = None, seq_len: int | tuple | None = None,
-                  head_weights: bool = True, dtype_gen_device: str | None = None,
-                  **overrides) -> SyntheticQSA:
+                  head_weights: bool = True, **overrides) -> SyntheticQSA:
     """Build the inputs of configuration ``name`` (see ``CONFIGS``).
 
     ``batch`` / ``seq_len`` / other keys override the configuration (tests use
@@ -187,7 +186,9 @@ def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
         token_to_req=token_to_req.to(device), query_start_loc=qsl.to(device), q=q, gate=gate,
         kv=kv, block_table=block_table.to(device), index_q=index_q, index_weights=weights,
         index_scale=di ** -0.5, index_cache=index_cache, index_table=index_table.to(device),
-        is_decode=is_decode, extra={"config": cfg})
+        is_decode=is_decode,
+        extra={"config": cfg, "max_seq_len": int(seq_lens.max()),
+               "max_query_len": int(q_lens.max())})
 
 
 __all__ = ["CONFIGS", "SyntheticQSA", "make_workload"]

@@ -24,7 +24,7 @@ import torch
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT / "tests"))
 
-from topk_cases import standard_cases  # noqa: E402
+from topk_cases import aligned_rows, standard_cases  # noqa: E402
 
 
 def main(out_path: str | None = None) -> None:
@@ -35,6 +35,7 @@ def main(out_path: str | None = None) -> None:
     dev = torch.device("cuda")
     for name, c in standard_cases().items():
         g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in c.items()}
+        g["scores"] = aligned_rows(g["scores"])   # the reference needs 16-byte aligned rows
         rows = c["scores"].shape[0]
         output = torch.full((rows, c["output_width"]), -7, dtype=torch.int32, device=dev)
         counts = torch.full((rows,), -7, dtype=torch.int32, device=dev)

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from oracle import qsa_oracle as O
-from topk_cases import make_case, standard_cases
+from topk_cases import aligned_rows, make_case, standard_cases
 
 pytestmark = pytest.mark.gpu
 
@@ -33,9 +33,17 @@ def dev():
     return torch.device("cuda")
 
 
-def run_topk_expand(case: dict, dev, col_stride: int = 1):
+def run_topk_expand(case: dict, dev, col_stride: int = 1, aligned: bool = False,
+                    score_offset: int = 0):
     from qsa_vllm_b200.topk import topk_expand
     g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    if aligned:
+        g["scores"] = aligned_rows(g["scores"])
+    if score_offset:
+        s = g["scores"]
+        buf = torch.zeros(s.shape[0], s.shape[1] + score_offset, dtype=s.dtype, device=dev)
+        buf[:, score_offset:] = s
+        g["scores"] = buf[:, score_offset:]
     rows = case["scores"].shape[0]
     width = case["output_width"]
     base = torch.full((rows, width * col_stride), -7, dtype=torch.int32, device=dev)
@@ -65,6 +73,16 @@ def test_topk_expand_matches_oracle(dev, name):
         assert np.array_equal(counts, ref_counts)
 
 
+def test_topk_expand_unaligned_score_rows(dev):
+    """Rows that are not 16-byte aligned take the scalar load path."""
+    case = make_case(22, 9, 777, 128, kind="relu")
+    ref, ref_counts = oracle_topk_expand(case)
+    for off in (0, 1, 3):
+        got, counts = run_topk_expand(case, dev, score_offset=off)
+        assert np.array_equal(got, ref), off
+        assert np.array_equal(counts, ref_counts)
+
+
 def test_topk_expand_strided_output(dev):
     case = make_case(21, 7, 3000, 512, kind="ties")
     got, _ = run_topk_expand(case, dev, col_stride=3)
@@ -74,9 +92,9 @@ def test_topk_expand_strided_output(dev):
 
 @pytest.mark.parametrize("rows,width,topk", [(1, 131072, 512), (8, 32768, 512),
                                              (64, 8192, 512), (300, 2048, 256),
-                                             (3, 70000, 4096)])
+                                             (3, 70000, 4096), (1, 200000, 2048)])
 def test_topk_expand_cluster_widths(dev, rows, width, topk):
-    """Cluster widths 1..16 CTAs per row (the launch plan depends on rows x width)."""
+    """Cluster widths 1..16 CTAs per row, 16 or 64 keys per thread (set by the width)."""
     for kind in ("relu", "ties"):
         case = make_case(rows * 7 + width, rows, width, topk * 4, kind=kind, lengths="full")
         got, counts = run_topk_expand(case, dev)
@@ -104,8 +122,9 @@ def test_topk_expand_matches_reference_cuda(dev):
     cases["decode_64x8192"] = make_case(77, 64, 8192, 2048, kind="relu", lengths="full")
     cases["decode_8x32768"] = make_case(78, 8, 32768, 2048, kind="relu", lengths="full")
     for name, case in cases.items():
-        got, counts = run_topk_expand(case, dev)
+        got, counts = run_topk_expand(case, dev, aligned=True)
         g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+        g["scores"] = aligned_rows(g["scores"])   # the reference needs 16-byte aligned rows
         rows = case["scores"].shape[0]
         out = torch.full((rows, case["output_width"]), -7, dtype=torch.int32, device=dev)
         cnt = torch.full((rows,), -7, dtype=torch.int32, device=dev)
@@ -218,6 +237,10 @@ def test_attention_matches_oracle(dev, rows, hq, hkv, d, physical, gate, counts)
     vc = torch.randint(0, width + 1, (rows,), generator=g).to(torch.int32) if counts else None
     if vc is not None:
         vc[0] = width
+        # Contract of valid_counts (what topk_expand writes): columns at or beyond
+        # the count hold -1.  The reference's kernel would also read valid ids
+        # there up to the end of its BLOCK_N tile, a schedule-dependent artifact.
+        idx[torch.arange(width)[None, :] >= vc[:, None]] = -1
     gt = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16) if gate else None
     kvd = kv.to(dev)
     out = torch.full((rows, hq, d), float("nan"), dtype=torch.bfloat16, device=dev)

@@ -73,6 +73,20 @@ def make_case(seed: int, rows: int, width: int, token_topk: int, *, ratio: int =
         output_width=token_topk + ratio - 1)
 
 
+def aligned_rows(scores: torch.Tensor) -> torch.Tensor:
+    """Same values in storage whose row stride is a multiple of 4 floats.
+
+    The reference selector reads score rows with float4 loads
+    (ops/csrc/topk.cu:80-88), so it requires 16-byte aligned rows; every
+    caller in the reference passes widths that are multiples of 64.  Inputs
+    handed to the reference checker are laid out this way.
+    """
+    rows, width = scores.shape
+    padded = torch.zeros(rows, -(-width // 4) * 4, dtype=scores.dtype, device=scores.device)
+    padded[:, :width] = scores
+    return padded[:, :width]
+
+
 def standard_cases() -> dict[str, dict]:
     """The named case set used by the parity tests and the golden fixtures."""
     c = {}
@@ -93,4 +107,4 @@ def standard_cases() -> dict[str, dict]:
     return c
 
 
-__all__ = ["make_case", "standard_cases"]
+__all__ = ["aligned_rows", "make_case", "standard_cases"]
