@@ -11,8 +11,9 @@ drop-in operators (``select_paged_tokens`` + ``qsa_sparse_paged_attention``)
 captured in a CUDA graph.  Inputs are synthetic (seeded N(0,1) / U(0,1)).
 
 Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on
-the launching stream, with the L2 flushed (256 MiB write) before every step
-outside the events; max over ranks.  With ``--gpus N`` (torchrun, NCCL) the
+the launching stream, with the L2 flushed before every step outside the
+events (a 256 MiB write, then a 256 MiB read of another buffer so the timed
+step does not pay for writing the flush's dirty lines back); max over ranks.  With ``--gpus N`` (torchrun, NCCL) the
 heads are sharded across ranks as vLLM tensor parallelism does (no
 collective inside the path; the indexer is replicated), so the total work is
 fixed: ``value`` = rows / (max-over-ranks step time).
@@ -64,7 +65,7 @@ def workload_desc(cfg: str, w) -> dict:
                      f"ratio {w.ratio}, top-k {w.token_topk} tokens, page {w.page_size}"),
         "global_batch": w.rows,
         "seq_len": c["seq_len"] if not isinstance(c["seq_len"], tuple) else list(c["seq_len"]),
-        "l2": "flushed before every timed step (256 MiB write, outside the events)",
+        "l2": "flushed before every timed step (256 MiB write + 256 MiB read, outside the events)",
         "cuda_graph": True,
     }
 
@@ -245,7 +246,12 @@ def main() -> None:
     idx_buf = torch.empty(rows, width, dtype=torch.int32, device=dev)
     cnt_buf = torch.empty(rows, dtype=torch.int32, device=dev)
     out = torch.empty_like(w.q)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_w = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_r = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        flush_w.zero_()   # evicts the previous step's lines (leaves dirty flush lines) ...
+        flush_r.sum()     # ... which a clean read then writes back, outside the timed region
 
     def step():
         select_paged_tokens(
@@ -274,7 +280,7 @@ def main() -> None:
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(k)]
         for a, b in evs:
-            flush.zero_()
+            flush_l2()
             a.record(stream)
             fn()
             b.record(stream)

@@ -14,7 +14,7 @@
  *   - Strides are in ELEMENTS of the pointed-to type, as torch reports them.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Nothing
  *     synchronises the host; every launch is CUDA-graph capturable.
- *   - No entry point allocates device memory.  Split-K attention takes a
+ *   - No entry point allocates device memory.  Attention takes a
  *     caller-provided workspace sized by qsa_sparse_attention_workspace_bytes.
  *   - Return value: QSA_OK or a QSA_ERR_* code; qsa_last_error() gives the
  *     detail for the calling host thread.  Invalid metadata VALUES (a -1 page,
@@ -130,8 +130,9 @@ QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_he
                        int64_t logits_row_stride, int32_t logits_width, void* stream);
 
 /*
- * Workspace bytes qsa_sparse_attention needs for these shapes (0 when the
- * launch plan uses a single split).  Deterministic in its arguments.
+ * Workspace bytes qsa_sparse_attention needs for these shapes on the current
+ * device: fp32 partial outputs + LSE of every (split, warp slot), combined by
+ * the merge pass.  Deterministic in its arguments for a given device.
  */
 QSA_API size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
                                             int32_t num_kv_heads, int32_t head_dim,

@@ -38,26 +38,34 @@
 namespace qsa {
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 6;
 constexpr int kGroups = 2;                        // consumer groups take alternate stages
 constexpr int kGroupWarps = 4;                    // warps per group: one (head, sub-tile) each
 constexpr int kConsumerWarps = kGroups * kGroupWarps;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kRing = 8;       // token-id ring slots (one per tile)
-constexpr int kLookahead = 4;  // tiles of token ids in flight ahead of the copies
+// Stage s is always consumed by group s % kGroups; with a stage count that is
+// not a multiple of kGroups, consecutive uses of a stage would alternate groups
+// and a group running two barrier phases ahead would alias the parity wait.
+static_assert(kStages % kGroups == 0, "each stage must belong to one consumer group");
+static_assert(kStages % kGroups == 0 && kGroups == 2, "producer p feeds consumer group p");
+constexpr int kThreads = (kConsumerWarps + kGroups) * 32;
+constexpr int kProducers = kGroups;  // producer warp p fills stages it % kProducers == p
+constexpr int kRing = 8;       // token-id ring slots per producer (one per own tile)
+constexpr int kLookahead = 4;  // own tiles of token ids in flight ahead of the copies
+static_assert(kLookahead < kRing, "ring / lookahead sizes");
 constexpr float kNegBig = -1.0e20f;
 
 template <int D, int NT, int HB>
 struct Smem {
-  static constexpr int kTT = 64 / HB;           // tokens per stage
-  static constexpr int kRow = HB * 4 * D + 16;  // K||V of HB heads + pad (bytes)
-  static constexpr int kQRows = HB * 8 * NT;    // staged query head rows per unit
-  alignas(128) uint8_t stage[kStages][kTT * kRow];
+  static constexpr int kTT = 64 / HB;            // tokens per stage
+  static constexpr int kRow = HB * 4 * D;        // K||V of HB heads of one token (bytes)
+  static constexpr int kBlk = 4 * kRow + 16;     // 4-token block + pad (bytes)
+  static constexpr int kQRows = HB * 8 * NT;     // staged query head rows per unit
+  // byte offset of token j of a stage: tokens are grouped in blocks of 4 that
+  // are copied whole when their slots are consecutive in the cache
+  static __device__ __forceinline__ int tok_off(int j) { return (j >> 2) * kBlk + (j & 3) * kRow; }
+  alignas(128) uint8_t stage[kStages][(kTT / 4) * kBlk];
   alignas(128) uint8_t q[2][kQRows * 2 * D];
-  float o_w[kConsumerWarps][8 * NT][D + 4];
-  float m_w[kConsumerWarps][8 * NT];
-  float l_w[kConsumerWarps][8 * NT];
-  int32_t ring[kRing][64];
+  int32_t ring[kGroups][kRing][64];
   uint64_t mask[kStages];
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -136,31 +144,34 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   const uint8_t* kbase = static_cast<const uint8_t*>(p.k_cache);
   const uint8_t* vbase = static_cast<const uint8_t*>(p.v_cache);
   const uint8_t* qbase = static_cast<const uint8_t*>(p.q);
+  const int pw = (threadIdx.x >> 5) - kConsumerWarps;  // this producer fills it % kProducers == pw
+  int32_t (*ring)[64] = sm.ring[pw];
 
-  Cursor<TT> ahead;
+  Cursor<TT> ahead;  // this producer's own tiles: positions pw, pw + kProducers, ...
   ahead.init(p, units, groups);
+  for (int i = 0; i < pw; ++i) ahead.next(p);
   auto prefetch = [&](int slot) {
     if (ahead.live) {
       const int32_t* idx_row = p.indices + static_cast<int64_t>(ahead.x.row) * p.indices_row_stride;
       for (int j = lane; j < TT; j += 32) {
         const int col = ahead.t * TT + j;
         const bool v = col < ahead.x.n_cols;
-        cp_async4(&sm.ring[slot][j], v ? idx_row + col : idx_row, v);
+        cp_async4(&ring[slot][j], v ? idx_row + col : idx_row, v);
       }
-      ahead.next(p);
+      for (int i = 0; i < kProducers; ++i) ahead.next(p);
     }
     cp_async_commit();
   };
 #pragma unroll 1
   for (int i = 0; i < kLookahead; ++i) prefetch(i % kRing);
 
-  int it = 0, k = 0;
+  int it = 0, k = 0, own = 0;
   bool ok = true;
   for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++k) {
     const Unit x = decode_unit<TT>(p, u, groups);
-    // ---- the unit's query rows -> q[k & 1]
+    // ---- the unit's query rows -> q[k & 1] (producer 0 only)
     const int qb = k & 1;
-    if (k >= 2 && !mbar_wait(&sm.qempty[qb], ((k >> 1) - 1) & 1)) {
+    if (pw == 0 && k >= 2 && !mbar_wait(&sm.qempty[qb], ((k >> 1) - 1) & 1)) {
       record_error(p.err, kDeviceErrWaitTimeout);
       sm.abort_flag = 1;
       ok = false;
@@ -169,7 +180,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     const int nq = HB * group;  // query head rows of this unit
     const uint8_t* qsrc = qbase + 2 * (static_cast<int64_t>(x.row) * p.q_row_stride +
                                        static_cast<int64_t>(x.hg * HB * group) * p.q_head_stride);
-    if (lane == 0) {
+    if (pw == 0 && lane == 0) {
       mbar_expect_tx(&sm.qfull[qb], static_cast<uint32_t>(nq * 2 * D));
       if (p.q_head_stride == D) {
         bulk_g2s(sm.q[qb], qsrc, static_cast<uint32_t>(nq * 2 * D), &sm.qfull[qb]);
@@ -190,6 +201,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         p.block_table + static_cast<int64_t>(req_ok ? req : 0) * p.table_row_stride;
     const int64_t head0 = static_cast<int64_t>(x.hg) * HB;
     for (int t = x.t0; t < x.t1; ++t, ++it) {
+      if (it % kProducers != pw) continue;  // the other producer's tile
       const int s = it % kStages;
       if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1)) {
         record_error(p.err, kDeviceErrWaitTimeout);
@@ -209,8 +221,9 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       // before the async-proxy (bulk copy) writes issued below
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       uint8_t* stage = sm.stage[s];
-      const int slot = it % kRing;
+      const int slot = own % kRing;
       int64_t off_k[2], off_v[2];
+      int slot_id[2];  // physical slot (page * page_size + offset), -1 when masked
       bool valid[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -219,7 +232,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         bool v = false;
         int page = 0, off = 0;
         if (j < TT && col < x.n_cols) {
-          const int tok = sm.ring[slot][j];
+          const int tok = ring[slot][j];
           int lp;
           p.page_div.divmod(max(tok, 0), lp, off);
           if (p.physical) {
@@ -232,30 +245,44 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
           }
         }
         valid[h] = v;
+        slot_id[h] = v ? page * p.page_size + off : -1;
         off_k[h] = static_cast<int64_t>(page) * p.k_block_stride +
                    static_cast<int64_t>(off) * p.k_token_stride + head0 * p.k_head_stride;
         off_v[h] = static_cast<int64_t>(page) * p.v_block_stride +
                    static_cast<int64_t>(off) * p.v_token_stride + head0 * p.v_head_stride;
         if (!v && j < TT) {  // masked token: zeros, as the reference's masked loads
-          uint4* z = reinterpret_cast<uint4*>(stage + j * kRow);
+          uint4* z = reinterpret_cast<uint4*>(stage + S::tok_off(j));
 #pragma unroll 4
-          for (int c = 0; c < (HB * 4 * D) / 16; ++c) z[c] = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < kRow / 16; ++c) z[c] = make_uint4(0, 0, 0, 0);
         }
       }
       const unsigned lo = __ballot_sync(0xffffffffu, valid[0]);
       const unsigned hi = __ballot_sync(0xffffffffu, valid[1]);
+      // A 4-token block whose slots are consecutive in a slot-contiguous cache
+      // is one run of 4*kRow bytes (4 selected tokens of one compressed block):
+      // copy it whole.  cont bit j: token j+1 is the slot after token j.
+      unsigned cont[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int nxt = __shfl_down_sync(0xffffffffu, slot_id[h], 1);
+        cont[h] = __ballot_sync(0xffffffffu, slot_id[h] >= 0 && nxt == slot_id[h] + 1);
+      }
       if (lane == 0) {
         sm.mask[s] = static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
-        mbar_expect_tx(&sm.full[s],
-                       static_cast<uint32_t>(__popc(lo) + __popc(hi)) * (HB * 4u * D));
+        mbar_expect_tx(&sm.full[s], static_cast<uint32_t>(__popc(lo) + __popc(hi)) * kRow);
       }
       __syncwarp();
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         if (!valid[h]) continue;
-        uint8_t* dst = stage + (lane + 32 * h) * kRow;
-        if (p.kv_fused == 2) {  // all HB heads' K||V rows contiguous
-          bulk_g2s(dst, kbase + 2 * off_k[h], HB * 4u * D, &sm.full[s]);
+        const int j = lane + 32 * h;
+        uint8_t* dst = stage + S::tok_off(j);
+        const bool whole = p.kv_fused == 2 && p.slot_contig && p.kv_heads == HB &&
+                           ((cont[h] >> (lane & ~3)) & 7u) == 7u;
+        if (whole) {
+          if ((lane & 3) == 0) bulk_g2s(dst, kbase + 2 * off_k[h], 4u * kRow, &sm.full[s]);
+        } else if (p.kv_fused == 2) {  // all HB heads' K||V rows of the token contiguous
+          bulk_g2s(dst, kbase + 2 * off_k[h], kRow, &sm.full[s]);
         } else {
 #pragma unroll 1
           for (int hh = 0; hh < HB; ++hh) {
@@ -272,17 +299,19 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         }
       }
       mbar_arrive(&sm.full[s]);
-      prefetch((it + kLookahead) % kRing);
+      prefetch((own + kLookahead) % kRing);
+      ++own;
     }
   }
   // Drain: never leave while a copy into this CTA's shared memory may be in
   // flight.  Wait (bounded) for the last issued phase of every barrier.
   cp_async_wait<0>();
   for (int j = std::max(0, it - kStages); j < it; ++j) {
+    if (j % kProducers != pw) continue;
     if (!mbar_wait(&sm.full[j % kStages], (j / kStages) & 1))
       record_error(p.err, kDeviceErrWaitTimeout);
   }
-  for (int j = std::max(0, k - 2); j < k; ++j) {
+  for (int j = std::max(0, k - 2); j < k && pw == 0; ++j) {
     if (!mbar_wait(&sm.qfull[j & 1], (j >> 1) & 1)) record_error(p.err, kDeviceErrWaitTimeout);
   }
 }
@@ -303,30 +332,38 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   const int group = p.q_heads / p.kv_heads;
   const float scale_log2 = p.scale_log2;
   const uint32_t stage0 = smem_u32(&sm.stage[0][0]);
-  constexpr uint32_t kStageBytes = TT * kRow;
+  constexpr uint32_t kStageBytes = (TT / 4) * S::kBlk;
+  // MMA row r (0..15) of this warp's sub-tile is token (r>>2) of block
+  // 4*sub + (r&3): the 8 rows of one ldmatrix span 4 blocks (2-way bank
+  // conflict at most; tokens of a block are contiguous, unpadded).
+  auto row_tok = [&](int r) { return (4 * sub + (r & 3)) * 4 + (r >> 2); };
   //   K (A operand of S^T, non-transposed): row = token, 16-byte chunk = dim/8
-  const uint32_t a_off = static_cast<uint32_t>((sub * 16 + (lane & 15)) * kRow + hh * 4 * D +
-                                               (lane >> 4) * 16);
-  //   V (A operand of O^T, transposed): {tok0-7,d0-7},{tok0-7,d8-15},{tok8-15,d0-7},{tok8-15,d8-15}
+  const uint32_t a_off =
+      static_cast<uint32_t>(S::tok_off(row_tok(lane & 15)) + hh * 4 * D + (lane >> 4) * 16);
+  //   V (A operand of O^T, transposed): {rows0-7,d0-7},{rows0-7,d8-15},{rows8-15,d0-7},{rows8-15,d8-15}
   const int mi = lane >> 3;
   const uint32_t v_off = static_cast<uint32_t>(
-      (sub * 16 + (lane & 7) + ((mi >> 1) << 3)) * kRow + hh * 4 * D + 2 * D + (mi & 1) * 16);
+      S::tok_off(row_tok((lane & 7) + ((mi >> 1) << 3))) + hh * 4 * D + 2 * D + (mi & 1) * 16);
 
+  // After a bounded wait expires (error recorded, abort flag raised) a warp
+  // neither waits nor computes any more, but it still walks every unit and
+  // reaches every named barrier, so no warp of the CTA is left waiting at one.
+  bool aborted = false;
   int it = 0, k = 0;
-  bool ok = true;
   for (int u = blockIdx.x; u < units; u += gridDim.x, ++k) {
     const Unit x = decode_unit<TT>(p, u, groups);
     const int qb = k & 1;
-    if (!mbar_wait(&sm.qfull[qb], (k >> 1) & 1)) {
+    aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
+    if (!aborted && !mbar_wait(&sm.qfull[qb], (k >> 1) & 1)) {
       record_error(p.err, kDeviceErrWaitTimeout);
       sm.abort_flag = 1;
-      break;
+      aborted = true;
     }
     // Q^T fragments (B operand of S^T): b0 = Q[head g][dims 2t4..], b1 = +8 dims.
     uint32_t qf[KS][NT][2];
     const uint8_t* qs = sm.q[qb];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < NT && !aborted; ++nt) {
       const int hl = g + 8 * nt;
       const bool hv = hl < group;
       const uint32_t* qrow =
@@ -338,7 +375,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.qempty[qb]);
+    if (lane == 0 && !aborted) mbar_arrive(&sm.qempty[qb]);
 
     float m[NT][2], l[NT][2];
     float o[KS][NT][4];
@@ -353,16 +390,28 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     for (int t = x.t0; t < x.t1; ++t, ++it) {
       if ((it % kGroups) != cg) continue;  // the other group's stage
       const int s = it % kStages;
+      aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
+      if (aborted) continue;
       if (!mbar_wait(&sm.full[s], (it / kStages) & 1)) {
         record_error(p.err, kDeviceErrWaitTimeout);
         sm.abort_flag = 1;
-        ok = false;
-        break;
+        aborted = true;
+        continue;
       }
       const uint64_t mask = sm.mask[s];
-      const bool v_lo = (mask >> (sub * 16 + g)) & 1ull;
-      const bool v_hi = (mask >> (sub * 16 + g + 8)) & 1ull;
+      const bool v_lo = (mask >> row_tok(g)) & 1ull;
+      const bool v_hi = (mask >> row_tok(g + 8)) & 1ull;
       const uint32_t sbase = stage0 + static_cast<uint32_t>(s) * kStageBytes;
+      // Pull this warp's K and V fragments into registers and hand the stage
+      // back to the producer at once: the stage is held only for the
+      // shared-memory reads, not for the math, so it is refilled sooner.
+      uint32_t ka[KS][4], va[KS][4];
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) ldsm_x4(ka[ks], sbase + a_off + ks * 32);
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) ldsm_x4_trans(va[mt], sbase + v_off + mt * 32);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[s]);
       // two independent accumulator chains (even / odd k-steps) halve the
       // dependent MMA latency of S^T
       float acc[NT][4], acc2[NT][4];
@@ -372,13 +421,10 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         for (int i = 0; i < 4; ++i) acc[nt][i] = acc2[nt][i] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < KS; ks += 2) {
-        uint32_t a[4], a2[4];
-        ldsm_x4(a, sbase + a_off + ks * 32);
-        ldsm_x4(a2, sbase + a_off + (ks + 1) * 32);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          mma_bf16(acc[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
-          mma_bf16(acc2[nt], a2, qf[ks + 1][nt][0], qf[ks + 1][nt][1]);
+          mma_bf16(acc[nt], ka[ks], qf[ks][nt][0], qf[ks][nt][1]);
+          mma_bf16(acc2[nt], ka[ks + 1], qf[ks + 1][nt][0], qf[ks + 1][nt][1]);
         }
       }
       uint32_t pb[NT][2];
@@ -412,18 +458,17 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) {
-        uint32_t a[4];
-        ldsm_x4_trans(a, sbase + v_off + mt * 32);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_bf16(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_bf16(o[mt][nt], va[mt], pb[nt][0], pb[nt][1]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[s]);
     }
-    if (!ok) break;
-    if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) break;
 
-    // ---- merge the warps holding each head (sub-tiles x groups), finish.
+    // ---- this warp's partial: normalized O and LSE of its heads over its
+    // tokens of the unit, written straight from registers (base-2 LSE, the
+    // reference's split-K format).  The merge kernel combines the partials of
+    // all (split, group, sub-tile) slots of a head.
+    if (aborted) continue;  // results of an aborted launch are not written
+    const int pslot = (x.split * kGroups + cg) * SUB + sub;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -433,68 +478,20 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         lv += __shfl_xor_sync(0xffffffffu, lv, 8);
         lv += __shfl_xor_sync(0xffffffffu, lv, 16);
         const int hl = 8 * nt + 2 * t4 + hc;
-        if (g == 0) {
-          sm.m_w[warp][hl] = m[nt][hc];
-          sm.l_w[warp][hl] = lv;
-        }
+        if (hl >= group) continue;
+        const bool has = lv > 0.f;
+        const float inv = has ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
+        const int head = (x.hg * HB + hh) * group + hl;
+        const int64_t base = (static_cast<int64_t>(pslot) * p.rows + x.row) * p.q_heads + head;
+        float* po = p.part_o + base * D;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          sm.o_w[warp][hl][mt * 16 + g] = o[mt][nt][hc];
-          sm.o_w[warp][hl][mt * 16 + g + 8] = o[mt][nt][2 + hc];
+          po[mt * 16 + g] = o[mt][nt][hc] * inv;
+          po[mt * 16 + g + 8] = o[mt][nt][2 + hc] * inv;
         }
+        if (g == 0) p.part_lse[base] = has ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
       }
     }
-    named_barrier(1, kConsumerWarps * 32);
-    const int per_head = group * (D / 2);
-    for (int e = threadIdx.x; e < HB * per_head; e += kConsumerWarps * 32) {
-      const int h2 = e / per_head;
-      const int rem = e % per_head;
-      const int hl = rem / (D / 2);
-      const int d0 = (rem % (D / 2)) * 2;
-      float M = kNegBig;
-#pragma unroll
-      for (int gi = 0; gi < kGroups; ++gi)
-#pragma unroll
-        for (int sb = 0; sb < SUB; ++sb)
-          M = fmaxf(M, sm.m_w[gi * kGroupWarps + h2 + HB * sb][hl]);
-      float L = 0.f, o0 = 0.f, o1 = 0.f;
-#pragma unroll
-      for (int gi = 0; gi < kGroups; ++gi) {
-#pragma unroll
-        for (int sb = 0; sb < SUB; ++sb) {
-          const int w = gi * kGroupWarps + h2 + HB * sb;
-          const float f = fast_exp2(sm.m_w[w][hl] - M);
-          L += sm.l_w[w][hl] * f;
-          o0 += sm.o_w[w][hl][d0] * f;
-          o1 += sm.o_w[w][hl][d0 + 1] * f;
-        }
-      }
-      const bool has = L > 0.f;
-      const float inv = has ? 1.f / fmaxf(L, 1.0e-20f) : 0.f;
-      o0 = has ? o0 * inv : 0.f;
-      o1 = has ? o1 * inv : 0.f;
-      const int head = (x.hg * HB + h2) * group + hl;
-      if (p.splits == 1) {
-        if (p.gate != nullptr) {
-          const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) +
-                                    static_cast<int64_t>(x.row) * p.gate_row_stride +
-                                    static_cast<int64_t>(head) * p.gate_head_stride;
-          const float g0 = __bfloat162float(gp[static_cast<int64_t>(d0) * p.gate_dim_stride]);
-          const float g1 = __bfloat162float(gp[static_cast<int64_t>(d0 + 1) * p.gate_dim_stride]);
-          o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-g0));
-          o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-g1));
-        }
-        __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
-                            static_cast<int64_t>(x.row) * p.out_row_stride +
-                            static_cast<int64_t>(head) * p.out_head_stride + d0;
-        *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(o0, o1);
-      } else {
-        const int64_t base = (static_cast<int64_t>(x.split) * p.rows + x.row) * p.q_heads + head;
-        *reinterpret_cast<float2*>(p.part_o + base * D + d0) = make_float2(o0, o1);
-        if (d0 == 0) p.part_lse[base] = has ? M + log2f(fmaxf(L, 1.0e-20f)) : -INFINITY;
-      }
-    }
-    named_barrier(1, kConsumerWarps * 32);
   }
 }
 
@@ -523,40 +520,83 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
     consumer<D, NT, HB>(p, sm, units, groups);
 }
 
-// Split merge (ops/qsa.py:306-362): one block per (row, query head).
+// Merge of the partial (normalized O, LSE) slots of every (row, query head):
+// the reference's split-K merge (ops/qsa.py:306-362) over the per-warp
+// partials of all splits, then bf16 rounding and the optional sigmoid gate.
+// One block per (row, 8 query heads), one warp per head, D/32 dims per lane;
+// the partial loop is unrolled so several slots' loads are in flight.
+constexpr int kMergeHeads = 8;
 template <int D>
-__global__ void __launch_bounds__(D / 2) merge_kernel(const AttnParams p) {
-  const int row = blockIdx.x, head = blockIdx.y;
-  const int d0 = threadIdx.x * 2;
+__global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParams p) {
+  constexpr int DPL = D / 32;  // dims per lane
+  const int row = blockIdx.x;
+  const int head = blockIdx.y * kMergeHeads + (threadIdx.x >> 5);
+  if (head >= p.q_heads) return;
+  const int d0 = (threadIdx.x & 31) * DPL;
+  const int64_t slot_stride = static_cast<int64_t>(p.rows) * p.q_heads;
+  const int64_t base = static_cast<int64_t>(row) * p.q_heads + head;
+  const int P = p.partials;
+  const int lane = threadIdx.x & 31;
+  // max LSE: the warp's lanes load 32 slots at a time
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s)
-    M = fmaxf(M, p.part_lse[(static_cast<int64_t>(s) * p.rows + row) * p.q_heads + head]);
-  float den = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int s0 = 0; s0 < P; s0 += 32)
+    if (s0 + lane < P) M = fmaxf(M, __ldg(p.part_lse + (s0 + lane) * slot_stride + base));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float den = 0.f;
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
   if (M > -INFINITY) {
-    for (int s = 0; s < p.splits; ++s) {
-      const int64_t base = (static_cast<int64_t>(s) * p.rows + row) * p.q_heads + head;
-      const float w = exp2f(p.part_lse[base] - M);
-      den += w;
-      const float2 v = *reinterpret_cast<const float2*>(p.part_o + base * D + d0);
-      o0 += v.x * w;
-      o1 += v.y * w;
+    // 8 slots per batch: all 16 loads are issued before any is used
+    for (int s0 = 0; s0 < P; s0 += 8) {
+      float lse[8];
+      float v[8][DPL];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t b = (s0 + j < P ? s0 + j : 0) * slot_stride + base;
+        lse[j] = s0 + j < P ? __ldg(p.part_lse + b) : -INFINITY;
+        const float* po = p.part_o + b * D + d0;
+        if constexpr (DPL == 4) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(po));
+          v[j][0] = t.x;
+          v[j][1] = t.y;
+          v[j][2] = t.z;
+          v[j][3] = t.w;
+        } else {
+          const float2 t = __ldg(reinterpret_cast<const float2*>(po));
+          v[j][0] = t.x;
+          v[j][1] = t.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float w = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
+        den += w;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * w;
+      }
     }
   }
-  o0 = den > 0.f ? o0 / den : 0.f;
-  o1 = den > 0.f ? o1 / den : 0.f;
-  if (p.gate != nullptr) {
-    const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) +
-                              static_cast<int64_t>(row) * p.gate_row_stride +
-                              static_cast<int64_t>(head) * p.gate_head_stride;
-    const float g0 = __bfloat162float(gp[static_cast<int64_t>(d0) * p.gate_dim_stride]);
-    const float g1 = __bfloat162float(gp[static_cast<int64_t>(d0 + 1) * p.gate_dim_stride]);
-    o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-g0));
-    o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-g1));
-  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
   __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
                       static_cast<int64_t>(row) * p.out_row_stride +
                       static_cast<int64_t>(head) * p.out_head_stride + d0;
-  *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(o0, o1);
+  const __nv_bfloat16* gp = p.gate == nullptr ? nullptr
+                            : static_cast<const __nv_bfloat16*>(p.gate) +
+                                  static_cast<int64_t>(row) * p.gate_row_stride +
+                                  static_cast<int64_t>(head) * p.gate_head_stride;
+#pragma unroll
+  for (int i = 0; i < DPL; i += 2) {
+    float o0 = acc[i] * inv, o1 = acc[i + 1] * inv;
+    if (gp != nullptr) {
+      const float g0 = __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride]);
+      const float g1 = __bfloat162float(gp[static_cast<int64_t>(d0 + i + 1) * p.gate_dim_stride]);
+      o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-g0));
+      o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-g1));
+    }
+    *reinterpret_cast<__nv_bfloat162*>(op + i) = __floats2bfloat162_rn(o0, o1);
+  }
 }
 
 template <int D, int NT, int HB>
@@ -570,8 +610,9 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
   const int grid = std::min(units, num_sms());
   attention_kernel<D, NT, HB><<<grid, kThreads, smem, stream>>>(p);
   e = cudaGetLastError();
-  if (e != cudaSuccess || p.splits == 1) return e;
-  merge_kernel<D><<<dim3(p.rows, p.q_heads), D / 2, 0, stream>>>(p);
+  if (e != cudaSuccess) return e;
+  merge_kernel<D><<<dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads), kMergeHeads * 32,
+                     0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -599,19 +640,11 @@ int attention_heads_per_unit(int q_heads, int kv_heads) {
   return 1;
 }
 
-AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
-                        int use_decode_kernel) {
-  (void)use_decode_kernel;
-  AttnPlan plan{1, 0};
-  const int hb = attention_heads_per_unit(q_heads, kv_heads);
-  const int tt = 64 / hb;
-  const int base = rows * (kv_heads / hb);
-  const int tiles = (topk_width + tt - 1) / tt;
-  const int G = num_sms();  // persistent grid: one CTA per SM, units dealt round-robin
-  if (base <= 0 || tiles <= 1 || base >= 4 * G) return plan;
-  // Simulate the round-robin deal for each split count and keep the one whose
-  // busiest CTA walks the fewest tiles (a unit's start + epilogue ~ three
-  // tiles; the merge launch ~ two tiles).
+// Split count for `base` units of `tiles` tiles on a persistent grid of G
+// CTAs that deals units round-robin: simulate the deal for each split count
+// and keep the one whose busiest CTA walks the fewest tiles (a unit's start
+// and epilogue ~ one tile; more partials make the merge ~ 1/8 tile each).
+int best_split(int base, int tiles, int G) {
   int best = 1;
   double best_cost = 1e30;
   const int max_split = std::min(tiles, 32);
@@ -622,22 +655,33 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
       double load = 0.0;
       for (int u = c; u < units; u += G) {
         const int sp = u % S;
-        load += ((sp + 1) * tiles / S - sp * tiles / S) + 3.0;
+        load += ((sp + 1) * tiles / S - sp * tiles / S) + 1.0;
       }
       worst = std::max(worst, load);
     }
-    const double cost = worst + (S > 1 ? 2.0 : 0.0);
+    const double cost = worst + 0.125 * S;
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = S;
     }
   }
-  plan.splits = best;
-  if (best > 1) {
-    const size_t o_bytes = static_cast<size_t>(best) * rows * q_heads * dim * sizeof(float);
-    const size_t l_bytes = static_cast<size_t>(best) * rows * q_heads * sizeof(float);
-    plan.workspace_bytes = ((o_bytes + 255) & ~static_cast<size_t>(255)) + l_bytes;
-  }
+  return best;
+}
+
+AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
+                        int use_decode_kernel) {
+  (void)use_decode_kernel;
+  AttnPlan plan{1, 0, 0};
+  const int hb = attention_heads_per_unit(q_heads, kv_heads);
+  const int tt = 64 / hb;
+  const int base = rows * (kv_heads / hb);
+  const int tiles = (topk_width + tt - 1) / tt;
+  const int G = num_sms();
+  if (base > 0 && tiles > 1 && base < 4 * G) plan.splits = best_split(base, tiles, G);
+  plan.partials = plan.splits * kGroups * (kGroupWarps / hb);
+  const size_t o_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * dim * sizeof(float);
+  const size_t l_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * sizeof(float);
+  plan.workspace_bytes = ((o_bytes + 255) & ~static_cast<size_t>(255)) + l_bytes;
   return plan;
 }
 

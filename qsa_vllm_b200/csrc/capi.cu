@@ -401,10 +401,13 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
                      k_block_stride == v_block_stride && k_token_stride == v_token_stride &&
                      k_head_stride == v_head_stride;
   p.kv_fused = fused ? (k_head_stride == 2 * head_dim ? 2 : 1) : 0;
+  p.slot_contig = k_block_stride == static_cast<int64_t>(page_size) * k_token_stride &&
+                  k_token_stride == static_cast<int64_t>(num_kv_heads) * k_head_stride;
   p.splits = plan.splits;
-  if (plan.splits > 1) {
+  p.partials = plan.partials;
+  {
     const size_t o_bytes =
-        static_cast<size_t>(plan.splits) * rows * num_q_heads * head_dim * sizeof(float);
+        static_cast<size_t>(plan.partials) * rows * num_q_heads * head_dim * sizeof(float);
     p.part_o = static_cast<float*>(workspace);
     p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                           ((o_bytes + 255) & ~static_cast<size_t>(255)));

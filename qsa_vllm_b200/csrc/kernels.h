@@ -92,13 +92,16 @@ struct AttnParams {
   float scale_log2;  // head_dim^-0.5 * log2(e), rounded once to fp32 (ops/qsa.py:176)
   int physical;
   int kv_fused;     // 2: K||V of consecutive heads contiguous; 1: per head; 0: apart
-  int splits;       // split-K factor per (row, kv head)
-  float* part_o;    // [splits, rows, q_heads, dim] fp32 (splits > 1)
-  float* part_lse;  // [splits, rows, q_heads] fp32
+  int slot_contig;  // consecutive slots are adjacent in memory (block stride = page * token stride)
+  int splits;       // split-K factor per (row, kv-head group)
+  int partials;     // partial (O, LSE) slots per (row, head) the merge combines
+  float* part_o;    // [partials, rows, q_heads, dim] fp32
+  float* part_lse;  // [partials, rows, q_heads] fp32
   int* err;
 };
 struct AttnPlan {
   int splits;
+  int partials;
   size_t workspace_bytes;
 };
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,

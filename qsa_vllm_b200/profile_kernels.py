@@ -8,8 +8,9 @@ Inputs are the synthetic workload of ``--config`` with ``--batch`` rows (the
 same per-row shapes as the benchmark, a smaller device footprint for ncu
 captures).  ``--contiguous-tables`` replaces the random block tables with the
 identity layout (each request's pages consecutive in memory), which isolates
-the cost of scattered pages.  ``--time`` prints CUDA-event timings with the L2
-flushed before every iteration.
+the cost of scattered pages.  ``--time`` prints CUDA-event timings of graph
+replays with the L2 flushed before every iteration (a 256 MiB write, then a
+256 MiB read so no dirty write-back lands in the timed region).
 """
 
 from __future__ import annotations
@@ -95,11 +96,13 @@ def main() -> None:
     with torch.cuda.graph(graph):
         fn()
     graph.replay()
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush_w = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush_r = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(a.iters)]
     for s, e in ev:
-        flush.zero_()
+        flush_w.zero_()  # evict, then read clean lines so no dirty write-back is timed
+        flush_r.sum()
         s.record()
         graph.replay()
         e.record()

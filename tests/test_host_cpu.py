@@ -73,7 +73,8 @@ def test_attention_workspace_query_is_deterministic():
     from qsa_vllm_b200.qsa import attention_workspace_bytes
     a = attention_workspace_bytes(64, 32, 4, 128, 2051, True)
     assert a == attention_workspace_bytes(64, 32, 4, 128, 2051, True)
-    assert attention_workspace_bytes(8192, 16, 2, 128, 1027, False) == 0
+    # per-warp partials (O, LSE) of every split are always merged by a second kernel
+    assert attention_workspace_bytes(8192, 16, 2, 128, 1027, False) > 0
 
 
 def test_operators_fail_loudly_without_a_gpu():
