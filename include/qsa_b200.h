@@ -130,6 +130,19 @@ QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_he
                        int64_t logits_row_stride, int32_t logits_width, void* stream);
 
 /*
+ * Visible compressed blocks per query row.
+ * Replaces the torch computation in select_paged_tokens (reference
+ * ops/indexer.py:363-369) with one launch:
+ *   visible[r] = token_to_req[r] in [0, num_requests)
+ *              ? min((positions[r] + 1) // ratio, sequence_lengths[req] // ratio) : 0
+ * with floor division as in torch.  positions: int64 [rows]; the rest int32.
+ * (The reference raises on token_to_req >= num_requests; here such rows get 0.)
+ */
+QSA_API int qsa_visible_blocks(const int64_t* positions, const int32_t* sequence_lengths,
+                               int32_t num_requests, const int32_t* token_to_req, int32_t rows,
+                               int32_t ratio, int32_t* visible, void* stream);
+
+/*
  * Workspace bytes qsa_sparse_attention needs for these shapes on the current
  * device: fp32 partial outputs + LSE of every (split, warp slot), combined by
  * the merge pass.  Deterministic in its arguments for a given device.

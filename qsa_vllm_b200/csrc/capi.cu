@@ -301,6 +301,20 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
   return QSA_OK;
 }
 
+int qsa_visible_blocks(const int64_t* positions, const int32_t* sequence_lengths,
+                       int32_t num_requests, const int32_t* token_to_req, int32_t rows,
+                       int32_t ratio, int32_t* visible, void* stream) {
+  const char* who = "qsa_visible_blocks";
+  if (rows < 0 || ratio <= 0) return fail(QSA_ERR_INVALID, "%s: bad rows / ratio", who);
+  if (rows == 0) return QSA_OK;
+  if (!positions || !sequence_lengths || !token_to_req || !visible)
+    return fail(QSA_ERR_INVALID, "%s: null pointer", who);
+  cudaError_t e = launch_visible_blocks(positions, sequence_lengths, num_requests, token_to_req,
+                                        rows, ratio, visible, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
 // -------------------------------------------------------------- attention
 size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
                                             int32_t num_kv_heads, int32_t head_dim,

@@ -15,6 +15,7 @@
 // weights in registers, reduces the heads of a row with warp shuffles and
 // stores coalesced fp32 logits.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -252,10 +253,18 @@ cudaError_t launch_d(const IndexerParams& p, int nt, dim3 grid, int rpc, int kpc
   return cudaErrorInvalidValue;
 }
 
+// QSA_INDEXER_MMA_SYNC=1 selects the mma.sync kernel for every shape (both
+// formulations compute the same scores; tests run the two against the oracle).
+bool indexer_force_mma() {
+  const char* v = std::getenv("QSA_INDEXER_MMA_SYNC");
+  return v != nullptr && v[0] == '1';
+}
+
 }  // namespace
 
 cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
   if (p.num_rows <= 0) return cudaSuccess;
+  if (indexer_tc_eligible(p) && !indexer_force_mma()) return launch_indexer_tc(p, stream);
   const bool decode = p.query_start_loc == nullptr;
   const int H = p.heads;
   int rows_per_cta, requests, row_tiles, keys_per_cta;
@@ -283,4 +292,38 @@ cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
   return cudaErrorInvalidValue;
 }
 
+}  // namespace qsa
+
+namespace qsa {
+namespace {
+// floor division (Python / torch `//` semantics), b > 0
+__device__ __forceinline__ long long floor_div(long long a, long long b) {
+  const long long q = a / b;
+  return (a % b != 0 && a < 0) ? q - 1 : q;
+}
+
+__global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* seq_lens,
+                                      int num_requests, const int32_t* token_to_req, int rows,
+                                      int ratio, int32_t* visible) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int req = token_to_req[r];
+  int v = 0;
+  if (req >= 0 && req < num_requests) {
+    const long long a = floor_div(positions[r] + 1, ratio);
+    const long long b = floor_div(seq_lens[req], ratio);
+    v = static_cast<int32_t>(a < b ? a : b);
+  }
+  visible[r] = v;
+}
+}  // namespace
+
+cudaError_t launch_visible_blocks(const int64_t* positions, const int32_t* seq_lens,
+                                  int num_requests, const int32_t* token_to_req, int rows,
+                                  int ratio, int32_t* visible, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  visible_blocks_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(
+      positions, seq_lens, num_requests, token_to_req, rows, ratio, visible);
+  return cudaGetLastError();
+}
 }  // namespace qsa

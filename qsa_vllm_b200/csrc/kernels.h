@@ -65,6 +65,13 @@ struct IndexerParams {
   int* err;
 };
 cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream);
+// tcgen05 + TMA formulation (indexer_tc.cu); launch_indexer dispatches to it
+// when indexer_tc_eligible() holds, else runs the mma.sync kernel.
+bool indexer_tc_eligible(const IndexerParams& p);
+cudaError_t launch_indexer_tc(const IndexerParams& p, cudaStream_t stream);
+cudaError_t launch_visible_blocks(const int64_t* positions, const int32_t* seq_lens,
+                                  int num_requests, const int32_t* token_to_req, int rows,
+                                  int ratio, int32_t* visible, cudaStream_t stream);
 
 // ------------------------------------------------------------- attention
 struct AttnParams {

@@ -36,6 +36,7 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 2048;
 constexpr int kMaxCluster = 16;
+constexpr int kMaxSelBytes = 192 * 1024;  // selected ids of one CTA: up to 49152 blocks
 
 struct RowMeta {
   int seq, complete, tail_start, tail_count;
@@ -168,6 +169,7 @@ template <int V>
 __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   constexpr int kChunks = V / 4;
   constexpr int kChunkKeys = 4 * kThreads;
+  extern __shared__ int sel[];  // selected column ids of this CTA, by rank (topk entries)
   __shared__ int hist[2][kBins];
   __shared__ int warp_tmp[kWarps];
   __shared__ int s_bin, s_remaining, s_bin_count;
@@ -308,6 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   }
   const int quota = min(max(remaining - ties_before, 0), tot_tie);
 
+  // Selection: each selected column id goes to sel[its rank - base_rank]
+  // (ascending column order = rank order, ties to the lowest columns).
   int run_strict = 0, run_tie = 0;
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
@@ -324,35 +328,30 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     const int ex = block_exclusive_sum((fs << 16) | ft, warp_tmp, round_total);
     int sb = run_strict + (ex >> 16);
     int tb = run_tie + (ex & 0xffff);
-    int rank[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t d = key[4 * c + j] >> shift;
       const bool v = valid_at(4 * c + j);
-      rank[j] = -1;
+      const int id = begin + 4 * (c * kThreads + tid) + j;
       if (v && d > prefix) {
-        rank[j] = base_rank + sb + min(tb, quota);
+        sel[sb + min(tb, quota)] = id;
         ++sb;
       } else if (v && d == prefix) {
-        if (tb < quota) rank[j] = base_rank + sb + tb;
+        if (tb < quota) sel[sb + tb] = id;
         ++tb;
       }
-      if (p.expand && rank[j] >= m.complete) rank[j] = -1;
     }
-    // page lookups of this thread's selected blocks first (independent loads),
-    // then the stores
-    int ph[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int id = begin + 4 * (c * kThreads + tid) + j;
-      ph[j] = (rank[j] >= 0 && p.expand && p.aligned_blocks) ? block_page(p, m, id * p.ratio) : 0;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (rank[j] >= 0)
-        store_block(p, m, out_row, rank[j], begin + 4 * (c * kThreads + tid) + j, ph[j]);
     run_strict += round_total >> 16;
     run_tie += round_total & 0xffff;
+  }
+  __syncthreads();
+  // Expansion: one rank per thread and iteration, so consecutive threads
+  // write consecutive output columns and issue their page lookups together.
+  const int mine = tot_strict + quota;
+  for (int i = tid; i < mine; i += kThreads) {
+    const int rank = base_rank + i;
+    if (p.expand && rank >= m.complete) break;
+    write_rank(p, m, out_row, rank, sel[i]);
   }
   if (crank == 0 && p.expand) finish_row(p, m, out_row, row);
   if (C > 1) cluster.sync();  // no CTA leaves while a peer may still read its shared memory
@@ -366,6 +365,11 @@ int pow2_ceil(int x) {
 
 template <int V>
 cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
+  const int smem = std::max(p.topk, 1) * static_cast<int>(sizeof(int));
+  if (smem > kMaxSelBytes) return cudaErrorInvalidValue;
+  cudaError_t e0 = set_attr_once(reinterpret_cast<const void*>(topk_kernel<V>),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSelBytes);
+  if (e0 != cudaSuccess) return e0;
   if (C > 8) {
     cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_kernel<V>),
                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -374,7 +378,7 @@ cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = static_cast<size_t>(std::max(p.topk, 1)) * sizeof(int);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

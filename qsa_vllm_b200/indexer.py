@@ -81,6 +81,27 @@ def indexer_scores(q: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Ten
             logits.shape[1], _lib.stream_ptr(q.device)), "indexer_scores")
 
 
+def compute_visible_blocks(query_positions: torch.Tensor, sequence_lengths: torch.Tensor,
+                           token_to_req: torch.Tensor, compress_ratio: int) -> torch.Tensor:
+    """min((pos + 1) // ratio, seq_len // ratio) per row, 0 for unmapped rows
+    (ops/indexer.py:363-369), in one sm_100a launch."""
+    rows = token_to_req.shape[0]
+    out = torch.empty(rows, dtype=torch.int32, device=token_to_req.device)
+    if rows == 0:
+        return out
+    _lib.ensure_device(token_to_req.device)
+    if query_positions.dtype != torch.int64 or sequence_lengths.dtype != torch.int32 \
+            or token_to_req.dtype != torch.int32:
+        raise TypeError("positions int64, sequence_lengths / token_to_req int32 expected")
+    lib = _lib.load_library()
+    with torch.cuda.device(token_to_req.device):
+        _lib.check(lib.qsa_visible_blocks(
+            query_positions.data_ptr(), sequence_lengths.data_ptr(), sequence_lengths.numel(),
+            token_to_req.data_ptr(), rows, int(compress_ratio), out.data_ptr(),
+            _lib.stream_ptr(token_to_req.device)), "visible_blocks")
+    return out
+
+
 def qsa_select_paged_decode(q, k_cache, page_table, visible_blocks, token_topk, compress_ratio,
                             decode_query_len, out, max_seq_len, *, query_positions,
                             sequence_lengths, token_to_req, main_block_table=None,
@@ -161,12 +182,8 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
     if not rows:
         return out
     if visible_blocks is None:
-        safe_requests = token_to_req.clamp_min(0).long()
-        visible_blocks = torch.minimum(
-            (query_positions + 1) // compress_ratio,
-            sequence_lengths.index_select(0, safe_requests) // compress_ratio,
-        ).to(torch.int32)
-        visible_blocks = torch.where(token_to_req >= 0, visible_blocks, 0)
+        visible_blocks = compute_visible_blocks(query_positions, sequence_lengths, token_to_req,
+                                                compress_ratio)
     if num_decode_tokens:
         qsa_select_paged_decode(
             q[:num_decode_tokens], k_cache, page_table[:num_decodes],
@@ -192,5 +209,5 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
     return out
 
 
-__all__ = ["indexer_scores", "qsa_select_paged_decode", "qsa_select_paged_prefill",
-           "select_paged_tokens"]
+__all__ = ["compute_visible_blocks", "indexer_scores", "qsa_select_paged_decode",
+           "qsa_select_paged_prefill", "select_paged_tokens"]

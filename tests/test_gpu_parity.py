@@ -154,11 +154,19 @@ def _indexer_case(dev, *, rows_per_req, requests, heads, dim, page, width, seed,
     return q, kc, table, vis, w
 
 
-@pytest.mark.parametrize("heads,dim,page,dql,weights", [
-    (8, 64, 64, 1, True), (4, 64, 16, 1, False), (4, 128, 16, 2, True), (16, 64, 32, 1, True),
-    (1, 64, 16, 1, False), (2, 128, 8, 4, False)])
-def test_indexer_decode_matches_oracle(dev, heads, dim, page, dql, weights):
+# page % 8 == 0 runs the tcgen05/TMA kernel, other pages (and mma_sync=True,
+# through QSA_INDEXER_MMA_SYNC=1) the mma.sync kernel
+@pytest.mark.parametrize("heads,dim,page,dql,weights,mma_sync", [
+    (8, 64, 64, 1, True, False), (4, 64, 16, 1, False, False), (4, 128, 16, 2, True, False),
+    (16, 64, 32, 1, True, False), (1, 64, 16, 1, False, False), (2, 128, 8, 4, False, False),
+    (64, 64, 64, 2, True, False), (48, 128, 24, 1, True, False), (8, 64, 128, 1, True, False),
+    (8, 64, 256, 1, True, False), (8, 64, 4, 1, True, False), (4, 128, 12, 2, True, False),
+    (8, 64, 64, 1, True, True), (4, 128, 16, 2, True, True)])
+def test_indexer_decode_matches_oracle(dev, monkeypatch, heads, dim, page, dql, weights,
+                                       mma_sync):
     from qsa_vllm_b200.indexer import indexer_scores
+    if mma_sync:
+        monkeypatch.setenv("QSA_INDEXER_MMA_SYNC", "1")
     q, kc, table, vis, w = _indexer_case(dev, rows_per_req=dql, requests=5, heads=heads, dim=dim,
                                          page=page, width=40, seed=heads * dim + page,
                                          weights=weights)
@@ -173,11 +181,15 @@ def test_indexer_decode_matches_oracle(dev, heads, dim, page, dql, weights):
     torch.testing.assert_close(got[m], ref[m], rtol=SCORE_RTOL, atol=SCORE_ATOL)
 
 
-@pytest.mark.parametrize("heads,dim", [(4, 64), (8, 64), (4, 128)])
-def test_indexer_prefill_matches_oracle(dev, heads, dim):
+@pytest.mark.parametrize("heads,dim,page,mma_sync", [
+    (4, 64, 16, False), (8, 64, 16, False), (4, 128, 16, False), (64, 64, 16, False),
+    (48, 128, 16, False), (8, 64, 64, False), (8, 64, 6, False), (8, 64, 16, True)])
+def test_indexer_prefill_matches_oracle(dev, monkeypatch, heads, dim, page, mma_sync):
     from qsa_vllm_b200.indexer import indexer_scores
-    g = torch.Generator().manual_seed(heads + dim)
-    page, width, requests = 16, 24, 3
+    if mma_sync:
+        monkeypatch.setenv("QSA_INDEXER_MMA_SYNC", "1")
+    g = torch.Generator().manual_seed(heads + dim + page)
+    width, requests = 384 // page, 3
     qlens = [70, 1, 45]
     qsl = torch.tensor([0, 70, 71, 116], dtype=torch.int32)
     rows = sum(qlens)
@@ -408,3 +420,14 @@ def test_prefill_step_cfg1(dev):
 def test_no_device_errors_recorded(dev):
     from qsa_vllm_b200 import _lib
     assert _lib.device_error_poll() == 0
+
+
+def test_visible_blocks_kernel_matches_reference_formula(dev):
+    from qsa_vllm_b200.indexer import compute_visible_blocks
+    g = torch.Generator().manual_seed(3)
+    seq = torch.randint(0, 5000, (9,), generator=g).to(torch.int32)
+    t2r = torch.randint(-1, 9, (300,), generator=g).to(torch.int32)
+    pos = torch.randint(-6, 6000, (300,), generator=g).to(torch.int64)
+    for ratio in (1, 4, 7):
+        got = compute_visible_blocks(pos.to(dev), seq.to(dev), t2r.to(dev), ratio).cpu()
+        assert torch.equal(got, O.visible_blocks(pos, seq, t2r, ratio))

@@ -237,6 +237,8 @@ def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch):
 
     monkeypatch.setattr(I, "indexer_scores", fake_scores)
     monkeypatch.setattr(I, "_topk_expand", fake_topk)
+    monkeypatch.setattr(I, "compute_visible_blocks",
+                        lambda pos, seq, t2r, ratio: O.visible_blocks(pos, seq, t2r, ratio))
     monkeypatch.setattr(I, "_INDEXER_WORKSPACE_BYTES", 3 * 64 * 4)   # force many chunks
     g = torch.Generator().manual_seed(0)
     ratio, page, topk = 4, 16, 32
