@@ -98,57 +98,76 @@ def algorithmic_bytes(w) -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled through
+    NVML every ~2 ms on a background thread while the timed region runs."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device: torch.device, period_s: float = 0.002):
+        self.device = device
+        self.period = period_s
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml as N
+        N.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            h = N.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            h = N.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+        self._nvml, self._handle = N, h
+        self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+
+    def _reasons(self) -> int:
+        N, h = self._nvml, self._handle
+        fn = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(h))
+
+    def _run(self):
+        import time as _t
+        N, h = self._nvml, self._handle
+        while not self._stop.is_set():
+            try:
+                self.samples.append((float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)),
+                                     self._reasons()))
+            except Exception:
+                pass
+            _t.sleep(self.period)
 
     def __enter__(self):
+        import threading
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            self._open()
+        except Exception:
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict | None:
-        if self.proc is None or not self.path:
+        if not self.samples:
             return None
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in Path(self.path).read_text().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 7:
-                continue
-            try:
-                sm.append(float(f[0]))
-                mx = float(f[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[3:7]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted({name for _, bits in self.samples for b, name in self.REASONS.items()
+                          if bits & b})
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+                "source": "NVML, every 2 ms during the timed region"}
 
 
 def cpu_baseline(cfg: str, rows: int = 4, min_seconds: float = 10.0) -> dict:
@@ -208,7 +227,7 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2_32k")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -234,8 +253,9 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
+    from qsa_vllm_b200 import _lib
     from qsa_vllm_b200.indexer import select_paged_tokens
-    from qsa_vllm_b200.qsa import attention_workspace_bytes, qsa_sparse_paged_attention
+    from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
     from qsa_vllm_b200.synthetic import make_workload
 
     full = make_workload(args.config, device=dev, seed=args.seed)
@@ -269,6 +289,12 @@ def main() -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
+    # kernels of one step, counted by the library at each launch (the graph
+    # replays exactly these)
+    n0 = _lib.kernel_launches()
+    step()
+    launches_per_step = _lib.kernel_launches() - n0
+    torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         step()
@@ -298,7 +324,7 @@ def main() -> None:
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         ms = timed(graph.replay, args.steps)
     torch.cuda.synchronize(dev)
     if dist is not None:
@@ -346,8 +372,6 @@ def main() -> None:
     tf = ROOT / "profiles" / "attention_cfg2_32k_traffic.json"
     if tf.exists() and world == 1 and args.config == "cfg2_32k":
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
-    need = attention_workspace_bytes(rows, w.q.shape[1], w.kv.shape[2], w.d, width, True)
-    launches_per_step = 3 + (1 if need else 0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -378,6 +402,7 @@ def main() -> None:
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
                 "api": "select_paged_tokens + qsa_sparse_paged_attention, eager"},
         "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches_per_step": launches_per_step,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -53,6 +53,12 @@ QSA_API const char* qsa_status_string(int status);
 QSA_API const char* qsa_last_error(void);
 /* Library version string. */
 QSA_API const char* qsa_version(void);
+/*
+ * Number of kernels this library has launched (or recorded into a CUDA graph)
+ * in this process, counted on the host at each successful launch.  No
+ * counterpart in the reference; used by benchmarks to report launches per step.
+ */
+QSA_API uint64_t qsa_kernel_launches(void);
 /* QSA_OK when the current device is sm_100; QSA_ERR_DEVICE otherwise. */
 QSA_API int qsa_device_check(void);
 /*

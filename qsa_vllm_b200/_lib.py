@@ -26,6 +26,7 @@ SIGNATURES: dict[str, tuple] = {
     "qsa_status_string": (C.c_char_p, [C.c_int]),
     "qsa_last_error": (C.c_char_p, []),
     "qsa_version": (C.c_char_p, []),
+    "qsa_kernel_launches": (C.c_uint64, []),
     "qsa_device_check": (C.c_int, []),
     "qsa_device_error_poll": (C.c_int, [C.POINTER(_i32)]),
     "qsa_topk_expand": (C.c_int, [
@@ -104,3 +105,8 @@ def device_error_poll() -> int:
 
 def version() -> str:
     return load_library().qsa_version().decode()
+
+
+def kernel_launches() -> int:
+    """Kernels launched (or recorded into CUDA graphs) by the library so far."""
+    return int(load_library().qsa_kernel_launches())

@@ -137,8 +137,8 @@ struct Cursor {
 template <int D, int NT, int HB>
 __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups) {
   using S = Smem<D, NT, HB>;
-  constexpr int TT = S::kTT;
   constexpr int kRow = S::kRow;
+  constexpr int TT = S::kTT;
   const int lane = threadIdx.x & 31;
   const int group = p.q_heads / p.kv_heads;
   const uint8_t* kbase = static_cast<const uint8_t*>(p.k_cache);
@@ -320,7 +320,6 @@ template <int D, int NT, int HB>
 __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups) {
   using S = Smem<D, NT, HB>;
   constexpr int TT = S::kTT;
-  constexpr int kRow = S::kRow;
   constexpr int SUB = kGroupWarps / HB;  // 16-token sub-tiles per stage per head
   constexpr int KS = D / 16;             // k-steps of S^T, m-tiles of O^T
   const int warp = threadIdx.x >> 5;
@@ -609,11 +608,11 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
   const int units = p.rows * (p.kv_heads / HB) * p.splits;
   const int grid = std::min(units, num_sms());
   attention_kernel<D, NT, HB><<<grid, kThreads, smem, stream>>>(p);
-  e = cudaGetLastError();
+  e = count_launches(cudaGetLastError());
   if (e != cudaSuccess) return e;
   merge_kernel<D><<<dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads), kMergeHeads * 32,
                      0, stream>>>(p);
-  return cudaGetLastError();
+  return count_launches(cudaGetLastError());
 }
 
 template <int D, int NT>

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <set>
 #include <tuple>
@@ -63,6 +64,13 @@ int* device_error_word() {
 }
 }  // namespace
 
+std::atomic<uint64_t> g_launches{0};
+
+cudaError_t count_launches(cudaError_t e, int n) {
+  if (e == cudaSuccess) g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed);
+  return e;
+}
+
 int num_sms() {
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return 148;
@@ -114,6 +122,8 @@ const char* qsa_status_string(int status) {
 const char* qsa_last_error(void) { return g_last_error; }
 
 const char* qsa_version(void) { return "qsa_b200 0.1.0 (sm_100a)"; }
+
+uint64_t qsa_kernel_launches(void) { return qsa::g_launches.load(std::memory_order_relaxed); }
 
 int qsa_device_check(void) {
   int dev = 0;
@@ -263,6 +273,9 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
       return fail(QSA_ERR_UNSUPPORTED, "%s: decode_query_len*heads > 128", who);
     if (query_offset != 0)
       return fail(QSA_ERR_INVALID, "%s: decode rows start at offset 0", who);
+    if (num_rows / decode_query_len > num_requests)
+      return fail(QSA_ERR_INVALID, "%s: %d decode requests but %d page-table rows", who,
+                  num_rows / decode_query_len, num_requests);
   } else if (num_requests <= 0 || max_query_len <= 0) {
     return fail(QSA_ERR_INVALID, "%s: prefill needs requests and max_query_len", who);
   }

@@ -36,6 +36,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
+// Arrive without release semantics: for a consumer that hands a buffer back
+// after it has finished reading it (no writes of its own to publish), so the
+// arrive need not wait for the thread's outstanding global stores.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.relaxed.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)

@@ -237,7 +237,7 @@ cudaError_t launch_dn(const IndexerParams& p, dim3 grid, int rows_per_cta, int k
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   indexer_kernel<D, NT><<<grid, kThreads, smem, stream>>>(p, rows_per_cta, keys_per_cta);
-  return cudaGetLastError();
+  return count_launches(cudaGetLastError());
 }
 
 template <int D>
@@ -264,7 +264,10 @@ bool indexer_force_mma() {
 
 cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
   if (p.num_rows <= 0) return cudaSuccess;
-  if (indexer_tc_eligible(p) && !indexer_force_mma()) return launch_indexer_tc(p, stream);
+  if (indexer_tc_eligible(p) && !indexer_force_mma()) {
+    const cudaError_t e = launch_indexer_tc(p, stream);
+    if (e != cudaErrorNotSupported) return e;  // else: tensor maps refused these strides
+  }
   const bool decode = p.query_start_loc == nullptr;
   const int H = p.heads;
   int rows_per_cta, requests, row_tiles, keys_per_cta;
@@ -324,6 +327,6 @@ cudaError_t launch_visible_blocks(const int64_t* positions, const int32_t* seq_l
   if (rows <= 0) return cudaSuccess;
   visible_blocks_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(
       positions, seq_lens, num_requests, token_to_req, rows, ratio, visible);
-  return cudaGetLastError();
+  return count_launches(cudaGetLastError());
 }
 }  // namespace qsa

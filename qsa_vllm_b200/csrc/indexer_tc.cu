@@ -4,29 +4,40 @@
 // (reference ops/indexer.py:24-114 decode, :117-223 prefill: bf16 inputs, fp32
 // products, ReLU per head, head sum, head_dim^-0.5).
 //
-// One CTA owns the query columns of a request (decode: its decode_query_len
-// rows; prefill: up to 128/H rows) and a chunk of that request's keys.
-//  * warp 0: TMA producer.  Key tiles of 128 keys are loaded page by page
-//    with 3-D tensor copies (dims: head dim, slot-in-page, physical page),
-//    128-byte swizzled, into a 4-stage shared-memory ring (mbarrier
-//    transaction counts).  An unmapped page is loaded through an
-//    out-of-bounds page coordinate, which the TMA unit fills with zeros.
+// Work decomposition.  A "segment" is the group of query rows that share one
+// page-table row and one B operand: a decode request (its decode_query_len
+// rows) or, in prefill, up to 128/H consecutive rows of one request.  Every
+// segment has at most T = ceil(capacity / 128) key tiles of 128 keys; the
+// (segment, tile) units are split into contiguous ranges, one per persistent
+// CTA (grid = resident CTAs of the whole GPU), so each CTA pays its set-up
+// once and streams keys through one continuous pipeline across segments.
+//
+// Roles (every role loop runs on the whole warp; one lane issues):
+//  * warp 0, producer: per segment, reads the rows' visible counts, writes
+//    the segment descriptor, head weights and column limits into one of two
+//    segment slots and loads the segment's query rows with a TMA tensor copy
+//    (128-byte swizzled, column n = row n/H, head n%H).  Then it loads the
+//    key tiles page by page with 3-D TMA copies (head dim, slot in page,
+//    physical page) into a ring of shared-memory stages.  Page ids come
+//    from a 32-page window of the table row held in registers, with the next
+//    window already in flight.  An unmapped page is read through an
+//    out-of-range page coordinate, which the TMA unit fills with zeros.
 //  * warp 1: allocates TMEM and issues tcgen05.mma (M = 128 keys, N = the
-//    CTA's query columns (rows x heads, padded to 16), K = 16 per
-//    instruction) into a double-buffered fp32 TMEM accumulator; completion
-//    is signalled with tcgen05.commit on mbarriers.
-//  * warps 2-5: epilogue.  Each thread owns one key (one TMEM lane):
-//    tcgen05.ld of its row of scores, ReLU, head weights, head sum, scale,
-//    and a coalesced fp32 store per query row.
-// Every wait is bounded; on expiry an error bit is recorded and the CTA
-// drains its copies and MMAs before releasing TMEM and returning.
+//    segment's query columns padded to 16, K = 16 per instruction) into a
+//    double-buffered fp32 accumulator; tcgen05.commit releases the stage and
+//    publishes the accumulator.
+//  * warps 2-5, epilogue: each thread owns one key (one TMEM lane) and,
+//    per tile, loads its scores with tcgen05.ld, applies ReLU, the head
+//    weights, the head sum and the scale, and stores one fp32 per query row
+//    (a warp writes 32 consecutive columns).
+// Every wait is bounded: on expiry the error word is set, the CTA stops
+// issuing work, waits (bounded) for its own copies and MMAs, releases TMEM
+// and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <map>
 #include <mutex>
-#include <tuple>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -34,40 +45,64 @@
 namespace qsa {
 namespace {
 
-constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
-constexpr int kTcStages = 4;
-constexpr int kTileKeys = 128;
-constexpr int kTcMaxKeysPerCta = 1024;
-constexpr int kTcMaxPages = kTcMaxKeysPerCta / 8 + 2;
+constexpr int kTileKeys = 128;  // keys per tcgen05.mma (M)
+constexpr int kEpiGroups = 2;   // epilogue warpgroups; group g takes stages g, g+2, ...
+constexpr int kTcThreads = (2 + 4 * kEpiGroups) * 32;  // producer, MMA, 8 epilogue warps
+
+struct SegMeta {
+  int r0;       // first absolute query row of the segment
+  int nrows;    // rows in the segment
+  int k_first;  // first key of this CTA's part of the segment
+  int nstages;  // key stages of this CTA's part; < 0 marks the end of the work
+};
+
+// Compile-time shape of one instantiation: head dim D, padded query columns NQ.
+template <int D, int NQ>
+struct TcCfg {
+  static constexpr int kSub = D / 64;                  // 128-byte sub-rows per key / query row
+  static constexpr int MT = D == 64 ? 2 : 1;           // 128-key MMA tiles per stage
+  static constexpr int kStageKeys = MT * kTileKeys;    // 256 keys (D=64) / 128 keys (D=128)
+  static constexpr int kSubBytes = kTileKeys * 128;    // one MMA tile, one sub-row: 16 KB
+  static constexpr int kStageBytes = MT * kSub * kSubBytes;  // 32 KB
+  static constexpr int kQSubBytes = NQ * 128;
+  // stages in flight: as many 32 KB stages as fit beside the two query slots
+  // (more bytes in flight per SM hide more DRAM latency)
+  static constexpr int kSmemBudget = 220 * 1024;
+  static constexpr int kFit = (kSmemBudget - 2 * kSub * kQSubBytes) / (MT * kSub * kTileKeys * 128);
+  static constexpr int S = kFit > 8 ? 8 : kFit;
+  static constexpr int kAccCols = MT * NQ;             // TMEM columns of one stage's scores
+  static constexpr int A = kAccCols <= 64 ? 4 : 2;     // accumulator ring (even: one group each)
+  static constexpr int kCols = A * kAccCols < 32 ? 32 : A * kAccCols;
+  static_assert(S >= 2, "stage ring too small");
+};
 
 template <int D, int NQ>
 struct TcSmem {
-  static constexpr int kSub = D / 64;                  // 128-byte sub-rows per key
-  static constexpr int kSubBytes = kTileKeys * 128;    // one sub-tile: 128 rows x 128 B
-  static constexpr int kStageBytes = kSub * kSubBytes;
-  alignas(1024) uint8_t k[kTcStages][kStageBytes];     // [sub][key][128 B], SW128
-  alignas(1024) uint8_t q[kSub][NQ * 128];             // [sub][column][128 B], SW128
-  float w[NQ];
-  int limit[NQ];
-  int pages[kTcMaxPages];
-  uint64_t full[kTcStages], empty[kTcStages], tfull[2], tempty[2];
+  using C = TcCfg<D, NQ>;
+  // stage layout: [mma tile m][sub][key row][128 B], each 128-key sub-tile 128B-swizzled
+  alignas(1024) uint8_t k[C::S][C::kStageBytes];
+  alignas(1024) uint8_t q[2][C::kSub][C::kQSubBytes];  // [slot][sub][column][128 B], swizzled
+  SegMeta meta[2];
+  float w[2][NQ];
+  int limit[2][NQ];  // per row of the segment: columns below this are stored
+  uint64_t full[C::S], empty[C::S], tfull[C::A], tempty[C::A], segfull[2], segempty[2];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle
+// UMMA shared-memory descriptor of a K-major operand in the 128-byte swizzle
 // atom layout: rows of 128 B, 8-row atoms 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
-  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused here)
+  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused: swizzled)
   d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: 8-row atoms
   d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
   d |= static_cast<uint64_t>(2) << 61;                  // layout: 128-byte swizzle
   return d;
 }
 
-// Instruction descriptor: D fp32, A/B bf16, both K-major, M x N.
+// Instruction descriptor of kind::f16: D fp32, A and B bf16, both K-major, M x N.
 template <int M, int N>
 constexpr uint32_t instr_desc() {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
@@ -81,6 +116,10 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -99,7 +138,7 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15}, [%16];"
@@ -109,206 +148,489 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// A read-only load that is issued exactly where it is written (the page-id
+// window is fetched ahead of its use).
+__device__ __forceinline__ int ld_once(const int32_t* ptr) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(ptr));
+  return v;
+}
+
+// Warp-uniform bounded wait: true when the phase completed for every lane.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+__device__ __forceinline__ bool aborted(const int* flag) {
+  return __any_sync(0xffffffffu, *reinterpret_cast<const volatile int*>(flag) != 0);
+}
+
+struct TcGeometry {
+  int segments;       // segment slots (prefill: requests x row tiles, some empty)
+  int row_tiles;      // prefill row tiles per request (1 for decode)
+  int rows_per_seg;   // rows of a full segment
+  int stages_per_seg; // key-stage upper bound per segment
+  int box_rows;       // key rows per TMA box (divides the page and 128)
+  int64_t units;      // segments x stages_per_seg
+};
+
+// Rows [r0, r1) of segment `seg` (absolute packed rows); r0 >= r1 if empty.
+__device__ __forceinline__ void segment_rows(const IndexerParams& p, const TcGeometry& g, int seg,
+                                             int& r0, int& r1) {
+  if (p.query_start_loc == nullptr) {
+    r0 = seg * p.decode_query_len;
+    r1 = r0 + p.decode_query_len;
+    return;
+  }
+  const int req = seg / g.row_tiles, rt = seg % g.row_tiles;
+  const int base = p.query_start_loc[0];
+  const int qend = p.query_offset + p.num_rows;
+  const int rs = max(p.query_start_loc[req] - base, p.query_offset);
+  const int re = min(p.query_start_loc[req + 1] - base, qend);
+  r0 = rs + rt * g.rows_per_seg;
+  r1 = min(r0 + g.rows_per_seg, re);
+}
+
+// Epilogue arithmetic, sequential form (any head count): ReLU, head weight,
+// sum of the H heads of each row, scaled store.  (acc, h, ri) carry a row
+// across calls.
+template <int N>
+__device__ __forceinline__ void score_columns_seq(const uint32_t* v, const float* wv, int c0,
+                                                  int H, float& acc, int& h, int& ri,
+                                                  int rows_here, const int* lim, float* out,
+                                                  int64_t row_stride, int key, float scale) {
+  float r[N];
+#pragma unroll
+  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+#pragma unroll
+  for (int x = 0; x < N; ++x) {
+    acc += r[x];
+    if (++h == H) {
+      if (ri < rows_here && key < lim[ri]) out[static_cast<int64_t>(ri) * row_stride + key] = acc * scale;
+      acc = 0.f;
+      h = 0;
+      ++ri;
+    }
+  }
+}
+
+// Power-of-two head count, all of a key's columns in one chunk, with the
+// segment's head weights and per-column store limits held in registers
+// (lim_col[n]: columns of key index below it are stored for column n's row;
+// 0 for padding rows).
+template <int N>
+__device__ __forceinline__ void score_columns_pow2_reg(const uint32_t* v, const float* wr,
+                                                       const int* lim_col, int H, int hshift,
+                                                       float* out, int64_t row_stride, int key,
+                                                       float scale) {
+  float r[N];
+#pragma unroll
+  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wr[x];
+#pragma unroll
+  for (int step = 1; step < N; step <<= 1) {
+    if (step < H) {
+#pragma unroll
+      for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+    }
+  }
+#pragma unroll
+  for (int x = 0; x < N; ++x)
+    if ((x & (H - 1)) == 0 && key < lim_col[x])
+      out[static_cast<int64_t>(x >> hshift) * row_stride + key] = r[x] * scale;
+}
+
+// Epilogue arithmetic for a power-of-two head count (H = 1 << hshift): the
+// heads of a row are summed by a log-depth tree over the chunk's columns
+// (every predicate is warp-uniform), then row sums are stored.  A row wider
+// than the chunk (H > N) is carried in `carry` and stored by its last chunk.
+template <int N>
+__device__ __forceinline__ void score_columns_pow2(const uint32_t* v, const float* wv, int c0,
+                                                   int H, int hshift, float& carry,
+                                                   int rows_here, const int* lim, float* out,
+                                                   int64_t row_stride, int key, float scale) {
+  float r[N];
+#pragma unroll
+  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+#pragma unroll
+  for (int step = 1; step < N; step <<= 1) {
+    if (step < H) {
+#pragma unroll
+      for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+    }
+  }
+  if (H <= N) {
+#pragma unroll
+    for (int x = 0; x < N; ++x) {
+      if ((x & (H - 1)) == 0) {
+        const int ri = (c0 + x) >> hshift;
+        if (ri < rows_here && key < lim[ri])
+          out[static_cast<int64_t>(ri) * row_stride + key] = r[x] * scale;
+      }
+    }
+  } else {
+    carry += r[0];
+    if (((c0 + N) & (H - 1)) == 0) {
+      const int ri = c0 >> hshift;
+      if (ri < rows_here && key < lim[ri])
+        out[static_cast<int64_t>(ri) * row_stride + key] = carry * scale;
+      carry = 0.f;
+    }
+  }
+}
+
 template <int D, int NQ>
 __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
-    const __grid_constant__ CUtensorMap kmap, const IndexerParams p, int rows_per_cta,
-    int keys_per_cta, int box_rows) {
-  using S = TcSmem<D, NQ>;
-  constexpr int kCols = 2 * NQ < 32 ? 32 : 2 * NQ;  // TMEM columns: two accumulators
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap qmap,
+    const IndexerParams p, const TcGeometry g) {
+  using C = TcCfg<D, NQ>;
+  using Sm = TcSmem<D, NQ>;
+  constexpr int S = C::S, A = C::A, MT = C::MT;
   constexpr uint32_t kIdesc = instr_desc<kTileKeys, NQ>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // the 128-byte swizzle pattern is taken from address bits: 1024-byte align
-  S& sm = *reinterpret_cast<S*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
+  Sm& sm = *reinterpret_cast<Sm*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = p.heads;
-
-  // ---- rows of this CTA (absolute packed rows) and their request.
-  const int req = blockIdx.x;
-  int r0, r1;
-  if (p.query_start_loc == nullptr) {
-    r0 = req * p.decode_query_len;
-    r1 = r0 + p.decode_query_len;
-  } else {
-    const int base = p.query_start_loc[0];
-    const int qend = p.query_offset + p.num_rows;
-    const int rs = max(p.query_start_loc[req] - base, p.query_offset);
-    const int re = min(p.query_start_loc[req + 1] - base, qend);
-    r0 = rs + blockIdx.y * rows_per_cta;
-    r1 = min(r0 + rows_per_cta, re);
-  }
-  if (r0 >= r1) return;
-  const int nrows = r1 - r0;
   const int cap = min(p.table_width * p.page_size, p.logits_width);
-  int maxvis = 0;
-  for (int i = 0; i < nrows; ++i) maxvis = max(maxvis, min(p.visible[r0 + i], cap));
-  const int k0 = blockIdx.z * keys_per_cta;
-  const int k1 = min(k0 + keys_per_cta, maxvis);
-  if (k0 >= k1) return;  // uniform: before any barrier or TMEM allocation
-  const int ntiles = (k1 - k0 + kTileKeys - 1) / kTileKeys;
 
-  // ---- setup: barriers, TMEM, query tile (swizzled), weights, page slice.
+  // this CTA's contiguous range of (segment, key stage) units
+  const int64_t ua = g.units * blockIdx.x / gridDim.x;
+  const int64_t ub = g.units * (blockIdx.x + 1) / gridDim.x;
+
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
+    for (int a = 0; a < A; ++a) {
+      mbar_init(&sm.tfull[a], 1);
+      mbar_init(&sm.tempty[a], 4);  // the four warps of the group that owns the buffer
+    }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.tfull[b], 1);
-      mbar_init(&sm.tempty[b], 4);
+      mbar_init(&sm.segfull[b], 1);
+      mbar_init(&sm.segempty[b], 4 * kEpiGroups);
     }
     sm.abort_flag = 0;
     fence_mbar_init();
   }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&qmap);
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
-                 "r"(kCols)
+                 "r"(C::kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid < NQ) {
-    const int ri = tid / H, h = tid % H;
-    const bool v = ri < nrows;
-    sm.w[tid] = v ? (p.weights ? p.weights[static_cast<int64_t>(r0 + ri) * p.w_row_stride +
-                                            static_cast<int64_t>(h) * p.w_head_stride]
-                               : 1.f)
-                  : 0.f;
-    sm.limit[tid] = tid < nrows ? min(p.visible[r0 + tid], cap) : 0;
-  }
-  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q);
-  for (int ch = tid; ch < NQ * (D / 8); ch += kTcThreads) {
-    const int n = ch / (D / 8), c16 = ch % (D / 8);  // column n, 16-byte chunk c16 of D*2 bytes
-    const int sub = c16 >> 3, c = c16 & 7;
-    const int ri = n / H, h = n % H;
-    const bool v = ri < nrows;
-    const __nv_bfloat16* src = qb + static_cast<int64_t>(v ? r0 + ri : r0) * p.q_row_stride +
-                               static_cast<int64_t>(v ? h : 0) * p.q_head_stride + c16 * 8;
-    cp_async16(sm.q[sub] + n * 128 + ((c ^ (n & 7)) << 4), src, v);
-  }
-  const int32_t* trow = p.table + static_cast<int64_t>(req) * p.table_row_stride;
-  const int pg0 = static_cast<int>(p.page_div.div(k0));
-  const int pg1 = static_cast<int>(p.page_div.div(k1 - 1));
-  for (int i = tid; i <= pg1 - pg0; i += kTcThreads) sm.pages[i] = trow[pg0 + i];
-  cp_async_commit();
-  cp_async_wait<0>();
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // q tile -> tensor-core reads
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const int boxes = kTileKeys / box_rows;
-      int t = 0;
-      for (; t < ntiles; ++t) {
-        const int s = t % kTcStages;
-        if (t >= kTcStages && !mbar_wait(&sm.empty[s], ((t / kTcStages) - 1) & 1)) {
-          record_error(p.err, kDeviceErrWaitTimeout);
-          sm.abort_flag = 1;
+    // ================================================================ producer
+    const int boxes = C::kStageKeys / g.box_rows;  // <= 32: one lane per box
+    const uint32_t qbytes = static_cast<uint32_t>(C::kSub * H * g.rows_per_seg * 128);
+    int it = 0;  // key stages issued (stage ring position)
+    int j = 0;   // segments published (slot ring position)
+    bool ok = true;
+    int64_t u = ua;
+    while (u < ub && ok) {
+      const int seg = static_cast<int>(u / g.stages_per_seg);
+      const int64_t seg_first = static_cast<int64_t>(seg) * g.stages_per_seg;
+      const int ta = static_cast<int>(u - seg_first);
+      const int64_t u_next = min(ub, seg_first + g.stages_per_seg);
+      const int tb0 = static_cast<int>(u_next - seg_first);
+      u = u_next;
+      int r0, r1;
+      segment_rows(p, g, seg, r0, r1);
+      if (r0 >= r1) continue;
+      const int nrows = r1 - r0;
+      const int table_row = p.query_start_loc == nullptr ? seg : seg / g.row_tiles;
+      const int32_t* trow = p.table + static_cast<int64_t>(table_row) * p.table_row_stride;
+      // All of the segment's metadata loads are issued before any is used:
+      // visible counts, head weights and a 64-page window of the table row
+      // (cur: pages wbase.., nxt: wbase+32..).  Pages past the visible keys
+      // may be read; their scores are never stored.
+      auto page_of = [&](int lp) { return lp < p.table_width ? ld_once(trow + lp) : -1; };
+      int wbase = static_cast<int>(p.page_div.div(ta * C::kStageKeys));
+      int cur = page_of(wbase + lane);
+      int nxt = page_of(wbase + 32 + lane);
+      int vis_lane[(NQ + 31) / 32];
+      float w_lane[(NQ + 31) / 32];
+#pragma unroll
+      for (int i = 0; i < (NQ + 31) / 32; ++i) {
+        const int n = lane + 32 * i;
+        const int ri = n / H, h = n - ri * H;
+        vis_lane[i] = n < nrows ? min(p.visible[r0 + n], cap) : 0;
+        w_lane[i] = 0.f;
+        if (n < NQ && ri < nrows)
+          w_lane[i] = p.weights ? p.weights[static_cast<int64_t>(r0 + ri) * p.w_row_stride +
+                                            static_cast<int64_t>(h) * p.w_head_stride]
+                                : 1.f;
+      }
+      int maxvis = 0;
+#pragma unroll
+      for (int i = 0; i < (NQ + 31) / 32; ++i) maxvis = max(maxvis, vis_lane[i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        maxvis = max(maxvis, __shfl_xor_sync(0xffffffffu, maxvis, o));
+      const int tb = min(tb0, (maxvis + C::kStageKeys - 1) / C::kStageKeys);
+      if (ta >= tb) continue;
+
+      // ---- publish the segment: descriptor, weights, limits, query rows
+      const int slot = j & 1;
+      if (aborted(&sm.abort_flag) ||
+          (j >= 2 && !warp_wait(&sm.segempty[slot], ((j >> 1) - 1) & 1))) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int i = 0; i < (NQ + 31) / 32; ++i) {
+        const int n = lane + 32 * i;
+        if (n < NQ) {
+          sm.w[slot][n] = w_lane[i];
+          sm.limit[slot][n] = vis_lane[i];
+        }
+      }
+      if (lane == 0) sm.meta[slot] = SegMeta{r0, nrows, ta * C::kStageKeys, tb - ta};
+      __syncwarp();
+      if (lane == 0) {
+        mbar_expect_tx(&sm.segfull[slot], qbytes);
+#pragma unroll
+        for (int sub = 0; sub < C::kSub; ++sub)
+          tma_load_3d(sm.q[slot][sub], &qmap, sub * 64, 0, r0, &sm.segfull[slot]);
+        mbar_arrive(&sm.segfull[slot]);
+      }
+      ++j;
+
+      // ---- key stages [ta, tb): lane b loads box b of each stage
+      const int box_key = lane * g.box_rows;  // this lane's box, relative to the stage
+      const int box_m = box_key / kTileKeys, box_row = box_key % kTileKeys;
+      for (int t = ta; t < tb; ++t) {
+        const int s = it % S;
+        if (aborted(&sm.abort_flag) ||
+            (it >= S && !warp_wait(&sm.empty[s], ((it / S) - 1) & 1))) {
+          ok = false;
           break;
         }
-        mbar_expect_tx(&sm.full[s], S::kStageBytes);
-        for (int bx = 0; bx < boxes; ++bx) {
-          const int key = k0 + t * kTileKeys + bx * box_rows;  // first key of the box
-          int lp, off;
-          p.page_div.divmod(key, lp, off);
-          int page = (lp <= pg1) ? sm.pages[lp - pg0] : -1;
-          if (page < 0 || page >= p.num_blocks) page = p.num_blocks;  // OOB: zero-filled
-#pragma unroll
-          for (int sub = 0; sub < S::kSub; ++sub)
-            tma_load_3d(sm.k[s] + sub * S::kSubBytes + bx * box_rows * 128, &kmap, sub * 64, off,
-                        page, &sm.full[s]);
+        const int key0 = t * C::kStageKeys;
+        if (static_cast<int>(p.page_div.div(key0)) >= wbase + 32) {  // at most one page in 32
+          wbase += 32;
+          cur = nxt;
+          nxt = page_of(wbase + 32 + lane);
         }
-        mbar_arrive(&sm.full[s]);
+        int lp, off;
+        p.page_div.divmod(key0 + box_key, lp, off);
+        const int d = lp - wbase;  // < 64: a stage spans at most 32 pages
+        const int pc = __shfl_sync(0xffffffffu, cur, d & 31);
+        const int pn = __shfl_sync(0xffffffffu, nxt, d & 31);
+        int page = d < 32 ? pc : pn;
+        if (page < 0 || page >= p.num_blocks) page = p.num_blocks;  // zero-filled
+        if (lane == 0) mbar_expect_tx(&sm.full[s], C::kStageBytes);
+        __syncwarp();
+        if (lane < boxes) {
+          uint8_t* dst = sm.k[s] + box_m * (C::kSub * C::kSubBytes) + box_row * 128;
+#pragma unroll
+          for (int sub = 0; sub < C::kSub; ++sub)
+            tma_load_3d(dst + sub * C::kSubBytes, &kmap, sub * 64, off, page, &sm.full[s]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.full[s]);
+        ++it;
       }
-      // drain: every issued tile has landed before the CTA may retire
-      for (int j = std::max(0, t - kTcStages); j < t; ++j)
-        if (!mbar_wait(&sm.full[j % kTcStages], (j / kTcStages) & 1))
-          record_error(p.err, kDeviceErrWaitTimeout);
     }
+    if (ok) {  // end marker in the next slot
+      const int slot = j & 1;
+      if (j >= 2 && !warp_wait(&sm.segempty[slot], ((j >> 1) - 1) & 1)) {
+        ok = false;
+      } else if (lane == 0) {
+        sm.meta[slot] = SegMeta{0, 0, 0, -1};
+        mbar_arrive(&sm.segfull[slot]);
+      }
+    }
+    if (!ok && lane == 0) {
+      record_error(p.err, kDeviceErrWaitTimeout);
+      sm.abort_flag = 1;
+    }
+    // drain: every copy this CTA issued has landed before it may retire
+    for (int x = max(0, it - S); x < it; ++x)
+      if (!warp_wait(&sm.full[x % S], (x / S) & 1) && lane == 0)
+        record_error(p.err, kDeviceErrWaitTimeout);
+    // query rows: with the end marker published, segment j-2's rows have
+    // landed (its slot was released by the epilogue) and its slot has moved
+    // on to the marker's phase, so only segment j-1 is waited for.
+    for (int x = max(0, ok ? j - 1 : j - 2); x < j; ++x)
+      if (!warp_wait(&sm.segfull[x & 1], (x >> 1) & 1) && lane == 0)
+        record_error(p.err, kDeviceErrWaitTimeout);
   } else if (warp == 1) {
-    // ------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      int t = 0;
-      for (; t < ntiles; ++t) {
-        const int s = t % kTcStages, b = t & 1;
-        if (!mbar_wait(&sm.full[s], (t / kTcStages) & 1) ||
-            (t >= 2 && !mbar_wait(&sm.tempty[b], ((t >> 1) - 1) & 1))) {
-          record_error(p.err, kDeviceErrWaitTimeout);
-          sm.abort_flag = 1;
+    // ================================================================ MMA issuer
+    int it = 0, j = 0;
+    bool ok = true;
+    while (ok) {
+      const int slot = j & 1;
+      if (aborted(&sm.abort_flag) || !warp_wait(&sm.segfull[slot], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const SegMeta m = sm.meta[slot];
+      if (m.nstages < 0) break;
+      const uint32_t qbase = smem_u32(sm.q[slot][0]);
+      for (int t = 0; t < m.nstages; ++t) {
+        const int s = it % S, a = it % A;
+        if (aborted(&sm.abort_flag) || !warp_wait(&sm.full[s], (it / S) & 1) ||
+            (it >= A && !warp_wait(&sm.tempty[a], ((it / A) - 1) & 1))) {
+          ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t kbase = smem_u32(sm.k[s]);
-        const uint32_t qbase = smem_u32(sm.q[0]);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int sub = kk >> 2, part = kk & 3;
-          const uint64_t ad = sw128_desc(kbase + sub * S::kSubBytes + part * 32);
-          const uint64_t bd = sw128_desc(qbase + sub * NQ * 128 + part * 32);
-          umma_bf16(tmem + b * NQ, ad, bd, kIdesc, kk > 0);
-        }
-        umma_commit(&sm.empty[s]);   // stage reusable once these MMAs have read it
-        umma_commit(&sm.tfull[b]);   // accumulator b ready for the epilogue
-      }
-      // drain: the last MMAs have completed before TMEM is released
-      if (t > 0 && !mbar_wait(&sm.tfull[(t - 1) & 1], ((t - 1) >> 1) & 1))
-        record_error(p.err, kDeviceErrWaitTimeout);
-    }
-  } else {
-    // ------------------------------------------------------ epilogue
-    const int quad = warp & 3;          // TMEM lanes 32*quad .. +31 = keys of this warp
-    const int key_in_tile = quad * 32 + lane;
-    const float scale = p.scale;
-    const int rows_here = NQ / H < nrows ? NQ / H : nrows;
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      // warp-uniform decisions: the tcgen05.ld below is .sync.aligned
-      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sm.abort_flag))) break;
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.tfull[b], (t >> 1) & 1))) {
         if (lane == 0) {
-          record_error(p.err, kDeviceErrWaitTimeout);
-          sm.abort_flag = 1;
+          const uint32_t kbase = smem_u32(sm.k[s]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int sub = kk >> 2, part = kk & 3;
+              const uint64_t ad = sw128_desc(kbase + (mt * C::kSub + sub) * C::kSubBytes + part * 32);
+              const uint64_t bd = sw128_desc(qbase + sub * C::kQSubBytes + part * 32);
+              umma_bf16(tmem + a * C::kAccCols + mt * NQ, ad, bd, kIdesc, kk > 0);
+            }
+          }
+          umma_commit(&sm.empty[s]);  // stage reusable once these MMAs have read it
+          umma_commit(&sm.tfull[a]);  // accumulator a ready for the epilogue
         }
+        __syncwarp();
+        ++it;
+      }
+      ++j;
+    }
+    if (!ok && lane == 0) {
+      record_error(p.err, kDeviceErrWaitTimeout);
+      sm.abort_flag = 1;
+    }
+    // drain: the last MMAs have completed before TMEM is released
+    if (it > 0 && !warp_wait(&sm.tfull[(it - 1) % A], ((it - 1) / A) & 1) && lane == 0)
+      record_error(p.err, kDeviceErrWaitTimeout);
+  } else {
+    // ================================================================ epilogue
+    const int grp = (warp - 2) >> 2;  // stages grp, grp + 2, ...
+    const int quad = warp & 3;        // TMEM lanes 32*quad .. +31 = keys of this warp
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const float scale = p.scale;
+    const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;  // log2(H), or -1
+    int it = 0, j = 0;
+    bool ok = true;
+    while (ok) {
+      const int slot = j & 1;
+      if (aborted(&sm.abort_flag) || !warp_wait(&sm.segfull[slot], (j >> 1) & 1)) {
+        ok = false;
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      // scores of this thread's key for all NQ columns, 16 columns per load;
-      // column n = (row n / H, head n % H): heads of a row are consecutive
-      const int key = k0 + t * kTileKeys + key_in_tile;
-      float acc = 0.f;
-      int h = 0, ri = 0;
+      const SegMeta m = sm.meta[slot];
+      if (m.nstages < 0) break;
+      const float* wv = sm.w[slot];
+      const int* lim = sm.limit[slot];
+      const int rows_here = min(NQ / H, m.nrows);
+      float* out = p.logits + static_cast<int64_t>(m.r0 - p.query_offset) * p.logits_row_stride;
+      // small shapes: the segment's weights and column limits in registers
+      constexpr bool kRegPath = C::kAccCols <= 32;
+      constexpr int kRegCols = kRegPath ? NQ : 1;
+      float wr[kRegCols];
+      int lim_col[kRegCols];
+      if constexpr (kRegPath) {
 #pragma unroll
-      for (int c = 0; c < NQ; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * NQ + c, v);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          acc += fmaxf(__uint_as_float(v[j]), 0.f) * sm.w[c + j];
-          if (++h == H) {
-            if (ri < rows_here && key < sm.limit[ri])
-              p.logits[static_cast<int64_t>(r0 + ri - p.query_offset) * p.logits_row_stride +
-                       key] = acc * scale;
-            acc = 0.f;
-            h = 0;
-            ++ri;
-          }
+        for (int x = 0; x < NQ; ++x) {
+          wr[x] = wv[x];
+          const int ri = hshift >= 0 ? x >> hshift : x / H;
+          lim_col[x] = ri < rows_here ? lim[ri] : 0;
         }
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      for (int t = 0; t < m.nstages; ++t, ++it) {
+        if ((it & 1) != grp) continue;
+        const int a = it % A;
+        if (aborted(&sm.abort_flag) || !warp_wait(&sm.tfull[a], (it / A) & 1)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int key0 = m.k_first + t * C::kStageKeys + quad * 32 + lane;
+        const uint32_t acc_base = tmem + lane_base + a * C::kAccCols;
+        constexpr int CH = C::kAccCols <= 64 ? NQ : 64;  // columns per arithmetic chunk
+        if constexpr (C::kAccCols <= 64) {
+          // all of this stage's columns in one round of loads
+          uint32_t v[C::kAccCols];
+#pragma unroll
+          for (int c = 0; c < C::kAccCols; c += 16) tmem_ld16(acc_base + c, v + c);
+          tmem_wait_ld();
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int key = key0 + mt * kTileKeys;
+            if (kRegPath && hshift >= 0) {
+              score_columns_pow2_reg<CH>(v + mt * NQ, wr, lim_col, H, hshift, out,
+                                         p.logits_row_stride, key, scale);
+            } else if (hshift >= 0) {
+              float carry = 0.f;
+              score_columns_pow2<CH>(v + mt * NQ, wv, 0, H, hshift, carry, rows_here, lim, out,
+                                     p.logits_row_stride, key, scale);
+            } else {
+              float acc = 0.f;
+              int h = 0, ri = 0;
+              score_columns_seq<CH>(v + mt * NQ, wv, 0, H, acc, h, ri, rows_here, lim, out,
+                                    p.logits_row_stride, key, scale);
+            }
+          }
+        } else {
+          // 64 columns per round of loads; a row may span rounds
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int key = key0 + mt * kTileKeys;
+            float acc = 0.f;
+            int h = 0, ri = 0;
+#pragma unroll
+            for (int c0 = 0; c0 < NQ; c0 += CH) {
+              uint32_t v[CH];
+#pragma unroll
+              for (int c = 0; c < CH; c += 16) tmem_ld16(acc_base + mt * NQ + c0 + c, v + c);
+              tmem_wait_ld();
+              if (hshift >= 0)
+                score_columns_pow2<CH>(v, wv, c0, H, hshift, acc, rows_here, lim, out,
+                                       p.logits_row_stride, key, scale);
+              else
+                score_columns_seq<CH>(v, wv, c0, H, acc, h, ri, rows_here, lim, out,
+                                      p.logits_row_stride, key, scale);
+            }
+          }
+        }
+        // the scores are in registers (tcgen05.wait::ld above): hand the
+        // accumulator back without waiting for this warp's logits stores
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_relaxed(&sm.tempty[a]);
+      }
+      if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.tempty[b]);
+      if (lane == 0) mbar_arrive(&sm.segempty[slot]);  // slot's rows, weights, limits done
+      ++j;
+    }
+    if (!ok && lane == 0) {
+      record_error(p.err, kDeviceErrWaitTimeout);
+      sm.abort_flag = 1;
     }
   }
+  // every role loop is warp-uniform, so each warp arrives here converged
   __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::kCols)
                  : "memory");
   }
 }
@@ -338,28 +660,38 @@ int gcd_int(int a, int b) {
 }
 
 template <int D, int NQ>
-cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& map, dim3 grid, int rpc, int kpc,
-                      int box_rows, cudaStream_t stream) {
+cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& kmap, const CUtensorMap& qmap,
+                      const TcGeometry& g, cudaStream_t stream) {
+  using C = TcCfg<D, NQ>;
+  const void* fn = reinterpret_cast<const void*>(indexer_tc_kernel<D, NQ>);
   const size_t smem = sizeof(TcSmem<D, NQ>) + 1024;  // + slack for 1024-byte alignment
-  cudaError_t e = set_attr_once(reinterpret_cast<const void*>(indexer_tc_kernel<D, NQ>),
-                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = set_attr_once(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  indexer_tc_kernel<D, NQ><<<grid, kTcThreads, smem, stream>>>(map, p, rpc, kpc, box_rows);
-  return cudaGetLastError();
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTcThreads, smem);
+  if (e != cudaSuccess) return e;
+  per_sm = std::max(1, std::min(per_sm, 512 / C::kCols));  // resident CTAs share 512 columns
+  const int64_t ctas = std::min<int64_t>(g.units, static_cast<int64_t>(num_sms()) * per_sm);
+  indexer_tc_kernel<D, NQ><<<static_cast<int>(ctas), kTcThreads, smem, stream>>>(kmap, qmap, p,
+                                                                                  g);
+  return count_launches(cudaGetLastError());
 }
 
 }  // namespace
 
 // Whether the tensor-core indexer takes these shapes (else the mma.sync path):
 // head dim 64 / 128, page size a multiple of 8 (whole 8-row swizzle atoms per
-// TMA box), 16-byte aligned strides, <= 128 query columns per CTA.
+// TMA box), 16-byte aligned rows and strides, <= 128 query columns per segment.
 bool indexer_tc_eligible(const IndexerParams& p) {
   if (p.dim != 64 && p.dim != 128) return false;
   if (p.heads <= 0 || p.heads > 128) return false;
   if (p.page_size % 8 != 0) return false;
   if ((p.token_stride * 2) % 16 != 0 || (p.block_stride * 2) % 16 != 0) return false;
   if (reinterpret_cast<uintptr_t>(p.k_cache) % 16 != 0) return false;
+  if (reinterpret_cast<uintptr_t>(p.q) % 16 != 0) return false;
+  if ((p.q_row_stride * 2) % 16 != 0) return false;
+  if (p.heads > 1 && (p.q_head_stride * 2) % 16 != 0) return false;
   if (p.num_blocks <= 0) return false;
   if (p.query_start_loc == nullptr && p.decode_query_len * p.heads > 128) return false;
   return tensor_map_encoder() != nullptr;
@@ -368,53 +700,72 @@ bool indexer_tc_eligible(const IndexerParams& p) {
 cudaError_t launch_indexer_tc(const IndexerParams& p, cudaStream_t stream) {
   const bool decode = p.query_start_loc == nullptr;
   const int H = p.heads;
-  int rows_per_cta, requests, row_tiles, keys_per_cta;
+  TcGeometry g{};
+  int q_rows;  // rows addressable through the query tensor map
   if (decode) {
-    rows_per_cta = p.decode_query_len;
-    requests = p.num_rows / p.decode_query_len;
-    row_tiles = 1;
-    keys_per_cta = kTcMaxKeysPerCta;
+    g.rows_per_seg = p.decode_query_len;
+    g.row_tiles = 1;
+    g.segments = p.num_rows / p.decode_query_len;
+    q_rows = p.num_rows;
   } else {
-    rows_per_cta = std::max(1, 128 / H);
-    requests = p.num_requests;
-    row_tiles = (std::min(p.num_rows, p.max_query_len) + rows_per_cta - 1) / rows_per_cta;
-    keys_per_cta = 512;
+    g.rows_per_seg = std::max(1, 128 / H);
+    g.row_tiles = (std::min(p.num_rows, p.max_query_len) + g.rows_per_seg - 1) / g.rows_per_seg;
+    g.segments = p.num_requests * g.row_tiles;
+    q_rows = p.query_offset + p.num_rows;
   }
-  const int n = rows_per_cta * H;
-  const int nq = n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128;
   const int cap = std::min(p.logits_width, p.table_width * p.page_size);
-  const int chunks = std::max(1, (cap + keys_per_cta - 1) / keys_per_cta);
-  if (requests <= 0 || row_tiles <= 0) return cudaSuccess;
-  const int box_rows = gcd_int(p.page_size, kTileKeys);
+  if (g.segments <= 0 || cap <= 0) return cudaSuccess;
+  const int stage_keys = p.dim == 64 ? TcCfg<64, 16>::kStageKeys : TcCfg<128, 16>::kStageKeys;
+  g.stages_per_seg = (cap + stage_keys - 1) / stage_keys;
+  g.units = static_cast<int64_t>(g.segments) * g.stages_per_seg;
+  g.box_rows = gcd_int(p.page_size, kTileKeys);
+  const int n = g.rows_per_seg * H;
+  const int nq = n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128;
 
-  // 3-D tensor map over the key cache: (head dim, slot in page, page).
-  CUtensorMap map;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim),
-                              static_cast<cuuint64_t>(p.page_size),
-                              static_cast<cuuint64_t>(p.num_blocks)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.token_stride) * 2,
-                                 static_cast<cuuint64_t>(p.block_stride) * 2};
-  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  // key cache: (head dim, slot in page, page); query rows: (head dim, head, row)
+  CUtensorMap kmap, qmap;
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = tensor_map_encoder()(
-      &map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p.k_cache), dims, strides,
-      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  const dim3 grid(requests, row_tiles, chunks);
+  {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim),
+                                static_cast<cuuint64_t>(p.page_size),
+                                static_cast<cuuint64_t>(p.num_blocks)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.token_stride) * 2,
+                                   static_cast<cuuint64_t>(p.block_stride) * 2};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(g.box_rows), 1};
+    if (tensor_map_encoder()(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                             const_cast<void*>(p.k_cache), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorNotSupported;
+  }
+  {
+    const int64_t hs = H == 1 ? p.dim : p.q_head_stride;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(q_rows)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hs) * 2,
+                                   static_cast<cuuint64_t>(p.q_row_stride) * 2};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(H),
+                               static_cast<cuuint32_t>(g.rows_per_seg)};
+    if (tensor_map_encoder()(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p.q),
+                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorNotSupported;
+  }
   if (p.dim == 64) {
     switch (nq) {
-      case 16: return launch_tc<64, 16>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-      case 32: return launch_tc<64, 32>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-      case 64: return launch_tc<64, 64>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-      default: return launch_tc<64, 128>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
+      case 16: return launch_tc<64, 16>(p, kmap, qmap, g, stream);
+      case 32: return launch_tc<64, 32>(p, kmap, qmap, g, stream);
+      case 64: return launch_tc<64, 64>(p, kmap, qmap, g, stream);
+      default: return launch_tc<64, 128>(p, kmap, qmap, g, stream);
     }
   }
   switch (nq) {
-    case 16: return launch_tc<128, 16>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-    case 32: return launch_tc<128, 32>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-    case 64: return launch_tc<128, 64>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
-    default: return launch_tc<128, 128>(p, map, grid, rows_per_cta, keys_per_cta, box_rows, stream);
+    case 16: return launch_tc<128, 16>(p, kmap, qmap, g, stream);
+    case 32: return launch_tc<128, 32>(p, kmap, qmap, g, stream);
+    case 64: return launch_tc<128, 64>(p, kmap, qmap, g, stream);
+    default: return launch_tc<128, 128>(p, kmap, qmap, g, stream);
   }
 }
 

@@ -116,6 +116,9 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
 
 int num_sms();
+// Counts `n` kernel launches of this library when `e` reports success (the
+// host-side count read by qsa_kernel_launches); returns `e`.
+cudaError_t count_launches(cudaError_t e, int n = 1);
 // cudaFuncSetAttribute(fn, attr, value) once per (function, attribute, device);
 // later launches (including ones under CUDA-graph capture) skip the call.
 cudaError_t set_attr_once(const void* fn, cudaFuncAttribute attr, int value);

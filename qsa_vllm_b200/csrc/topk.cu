@@ -387,7 +387,7 @@ cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, topk_kernel<V>, p);
+  return count_launches(cudaLaunchKernelEx(&cfg, topk_kernel<V>, p));
 }
 
 }  // namespace

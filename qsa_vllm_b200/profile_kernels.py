@@ -57,9 +57,13 @@ def main() -> None:
     cnt = torch.empty(rows, dtype=torch.int32, device=dev)
     out = torch.empty_like(w.q)
 
+    # decode rows: one page-table row per request; prefill: packed rows
+    prefill = {} if w.is_decode else dict(query_start_loc=w.query_start_loc,
+                                          max_query_len=w.max_query_len)
+
     def run_indexer():
         indexer_scores(w.index_q, w.index_cache, w.index_table, vis, logits,
-                       weights=w.index_weights, scale=w.index_scale)
+                       weights=w.index_weights, scale=w.index_scale, **prefill)
 
     def run_topk():
         topk_expand(logits, vis, w.positions, w.seq_lens, w.token_to_req, idx, r,

@@ -211,6 +211,65 @@ def test_indexer_prefill_matches_oracle(dev, monkeypatch, heads, dim, page, mma_
         torch.testing.assert_close(got[m], ref[m], rtol=SCORE_RTOL, atol=SCORE_ATOL)
 
 
+def test_indexer_decode_many_segments_per_cta(dev):
+    """More (request, key tile) units than resident CTAs: each persistent CTA
+    walks several requests (segment slots reused) with random visible counts."""
+    from qsa_vllm_b200.indexer import indexer_scores
+    q, kc, table, vis, w = _indexer_case(dev, rows_per_req=1, requests=300, heads=8, dim=64,
+                                         page=16, width=24, seed=11, weights=True)
+    vis[::7] = 0
+    cols = 24 * 16
+    logits = torch.full((q.shape[0], cols), float("nan"), device=dev)
+    indexer_scores(q.to(dev), kc.to(dev), table.to(dev), vis.to(dev), logits, weights=w.to(dev))
+    ref = O.indexer_scores(q, kc, table, vis, cols, weights=w)
+    got = logits.cpu()
+    assert torch.equal(torch.isnan(got), torch.isnan(ref))
+    m = ~torch.isnan(ref)
+    torch.testing.assert_close(got[m], ref[m], rtol=SCORE_RTOL, atol=SCORE_ATOL)
+
+
+@pytest.mark.parametrize("heads,dim", [(8, 64), (4, 128)])
+def test_indexer_prefill_many_row_tiles(dev, heads, dim):
+    """Long prefill requests: many row tiles per request, partial last tiles."""
+    from qsa_vllm_b200.indexer import indexer_scores
+    g = torch.Generator().manual_seed(7 + heads)
+    page, width = 32, 12
+    qlens = [333, 17, 250]
+    qsl = torch.tensor([0, 333, 350, 600], dtype=torch.int32)
+    rows, requests = sum(qlens), len(qlens)
+    nblk = requests * width + 5
+    q = (torch.randn(rows, heads, dim, generator=g) * dim ** -0.5).to(torch.bfloat16)
+    kc = torch.randn(nblk, page, 1, dim, generator=g).to(torch.bfloat16)
+    table = torch.randperm(nblk, generator=g)[: requests * width].view(requests, width)
+    table = table.to(torch.int32).contiguous()
+    vis = torch.randint(0, width * page + 1, (rows,), generator=g).to(torch.int32)
+    w = torch.rand(rows, heads, generator=g)
+    lw = width * page
+    for qoff, nq in ((0, rows), (100, 333)):
+        logits = torch.full((nq, lw), float("nan"), device=dev)
+        indexer_scores(q.to(dev), kc.to(dev), table.to(dev), vis.to(dev), logits,
+                       query_start_loc=qsl.to(dev), max_query_len=333, query_offset=qoff,
+                       num_rows=nq, weights=w.to(dev))
+        ref = O.indexer_scores(q, kc, table, vis, lw, query_start_loc=qsl, weights=w)
+        ref = ref[qoff:qoff + nq]
+        got = logits.cpu()
+        assert torch.equal(torch.isnan(got), torch.isnan(ref))
+        m = ~torch.isnan(ref)
+        torch.testing.assert_close(got[m], ref[m], rtol=SCORE_RTOL, atol=SCORE_ATOL)
+
+
+def test_indexer_rejects_decode_rows_without_table_rows(dev):
+    """Decode rows need one page-table row per request: the call is refused on
+    the host before any launch (no out-of-range table reads)."""
+    from qsa_vllm_b200._lib import QSAError
+    from qsa_vllm_b200.indexer import indexer_scores
+    q, kc, table, vis, _ = _indexer_case(dev, rows_per_req=1, requests=4, heads=8, dim=64,
+                                         page=16, width=8, seed=5, weights=False)
+    logits = torch.zeros(q.shape[0], 8 * 16, device=dev)
+    with pytest.raises(QSAError, match="page-table rows"):
+        indexer_scores(q.to(dev), kc.to(dev), table[:2].to(dev), vis.to(dev), logits)
+
+
 # ---------------------------------------------------------------- attention
 def _attention_check(got: torch.Tensor, ref: torch.Tensor):
     got = got.float().cpu()
