@@ -192,6 +192,35 @@ QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_
                          int32_t use_decode_kernel, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/*
+ * qsa_sparse_attention for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same arguments and results as
+ * qsa_sparse_attention without (workspace, workspace_bytes): the split-K
+ * scratch is a file-scope device array of QSA_STATIC_SCRATCH_BYTES per device,
+ * whose address is resolved once per device; nothing is allocated.
+ *   - Calls needing more scratch than QSA_STATIC_SCRATCH_BYTES (see
+ *     qsa_sparse_attention_workspace_bytes; 18 MiB for 64 decode rows of
+ *     32 query / 4 KV heads x 128 at top-k 2048) return QSA_ERR_WORKSPACE.
+ *   - Nothing in the scratch has to start at zero: each call writes every
+ *     partial slot it reads.
+ *   - One scratch array serves all calls on a device: calls whose kernels
+ *     overlap on the GPU (other streams or host threads) race on it; the
+ *     caller must serialise them.
+ */
+#define QSA_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
+QSA_API int qsa_sparse_attention_static_scratch(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, int32_t rows,
+    int32_t num_q_heads, int32_t head_dim, const void* k_cache, int64_t k_block_stride,
+    int64_t k_token_stride, int64_t k_head_stride, const void* v_cache, int64_t v_block_stride,
+    int64_t v_token_stride, int64_t v_head_stride, int32_t num_blocks, int32_t page_size,
+    int32_t num_kv_heads, const int32_t* indices, int64_t indices_row_stride,
+    int32_t topk_width, const int32_t* block_table, int64_t table_row_stride,
+    int32_t table_width, int32_t num_requests, const int32_t* token_to_req,
+    const int32_t* valid_counts, const void* gate, int64_t gate_row_stride,
+    int64_t gate_head_stride, int64_t gate_dim_stride, void* out, int64_t out_row_stride,
+    int64_t out_head_stride, int32_t indices_are_physical, int32_t use_decode_kernel,
+    void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -64,6 +64,14 @@ int* device_error_word() {
 }
 }  // namespace
 
+int set_last_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
 std::atomic<uint64_t> g_launches{0};
 
 cudaError_t count_launches(cudaError_t e, int n) {

@@ -119,6 +119,9 @@ int num_sms();
 // Counts `n` kernel launches of this library when `e` reports success (the
 // host-side count read by qsa_kernel_launches); returns `e`.
 cudaError_t count_launches(cudaError_t e, int n = 1);
+// Records a failure message for qsa_last_error() on this host thread and
+// returns `status` (for entry points outside capi.cu).
+int set_last_error(int status, const char* fmt, ...);
 // cudaFuncSetAttribute(fn, attr, value) once per (function, attribute, device);
 // later launches (including ones under CUDA-graph capture) skip the call.
 cudaError_t set_attr_once(const void* fn, cudaFuncAttribute attr, int value);

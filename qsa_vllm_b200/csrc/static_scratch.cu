@@ -1,0 +1,84 @@
+// qsa_sparse_attention_static_scratch: paged sparse attention for callers that
+// cannot allocate device memory.  The split-K workspace (normalised partial
+// outputs + LSE) lives in a file-scope device array of QSA_STATIC_SCRATCH_BYTES
+// instead of a caller-provided buffer; nothing here allocates.
+//
+// Nothing in the scratch must start at zero: every partial slot the merge
+// reads is written by the main kernel of the same call, so no clearing pass is
+// needed.  There is one scratch array per device, shared by every call on that
+// device: calls whose kernels overlap on the GPU (other streams, other host
+// threads) race on it and must be serialised by the caller.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/qsa_b200.h"
+#include "kernels.h"
+
+namespace {
+
+constexpr size_t kScratchBytes = QSA_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxScratchDevices] = {};
+
+// Device address of this device's scratch: resolved once per device, with
+// that device current.
+cudaError_t scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int qsa_sparse_attention_static_scratch(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, int32_t rows,
+    int32_t num_q_heads, int32_t head_dim, const void* k_cache, int64_t k_block_stride,
+    int64_t k_token_stride, int64_t k_head_stride, const void* v_cache, int64_t v_block_stride,
+    int64_t v_token_stride, int64_t v_head_stride, int32_t num_blocks, int32_t page_size,
+    int32_t num_kv_heads, const int32_t* indices, int64_t indices_row_stride,
+    int32_t topk_width, const int32_t* block_table, int64_t table_row_stride,
+    int32_t table_width, int32_t num_requests, const int32_t* token_to_req,
+    const int32_t* valid_counts, const void* gate, int64_t gate_row_stride,
+    int64_t gate_head_stride, int64_t gate_dim_stride, void* out, int64_t out_row_stride,
+    int64_t out_head_stride, int32_t indices_are_physical, int32_t use_decode_kernel,
+    void* stream) {
+  const char* who = "qsa_sparse_attention_static_scratch";
+  if (rows > 0 && num_q_heads > 0 && num_kv_heads > 0 && head_dim > 0 && topk_width >= 0) {
+    const size_t need = qsa_sparse_attention_workspace_bytes(
+        rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel);
+    if (need > kScratchBytes)
+      return qsa::set_last_error(
+          QSA_ERR_WORKSPACE,
+          "%s: this call needs %zu bytes of split-K scratch, above the static maximum of %zu "
+          "bytes (QSA_STATIC_SCRATCH_BYTES); use qsa_sparse_attention with a caller workspace",
+          who, need, kScratchBytes);
+  }
+  void* scratch = nullptr;
+  const cudaError_t e = scratch_address(&scratch);
+  if (e != cudaSuccess)
+    return qsa::set_last_error(QSA_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who,
+                               cudaGetErrorString(e));
+  return qsa_sparse_attention(q, q_row_stride, q_head_stride, rows, num_q_heads, head_dim,
+                              k_cache, k_block_stride, k_token_stride, k_head_stride, v_cache,
+                              v_block_stride, v_token_stride, v_head_stride, num_blocks,
+                              page_size, num_kv_heads, indices, indices_row_stride, topk_width,
+                              block_table, table_row_stride, table_width, num_requests,
+                              token_to_req, valid_counts, gate, gate_row_stride,
+                              gate_head_stride, gate_dim_stride, out, out_row_stride,
+                              out_head_stride, indices_are_physical, use_decode_kernel, scratch,
+                              kScratchBytes, stream);
+}
