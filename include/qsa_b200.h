@@ -199,7 +199,7 @@ QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_
  * scratch is a file-scope device array of QSA_STATIC_SCRATCH_BYTES per device,
  * whose address is resolved once per device; nothing is allocated.
  *   - Calls needing more scratch than QSA_STATIC_SCRATCH_BYTES (see
- *     qsa_sparse_attention_workspace_bytes; 18 MiB for 64 decode rows of
+ *     qsa_sparse_attention_workspace_bytes; 8 MiB for 64 decode rows of
  *     32 query / 4 KV heads x 128 at top-k 2048) return QSA_ERR_WORKSPACE.
  *   - Nothing in the scratch has to start at zero: each call writes every
  *     partial slot it reads.

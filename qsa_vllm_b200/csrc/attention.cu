@@ -9,8 +9,10 @@
 //
 // Design (B200).  The work is a gather at 8 flop/byte, so the kernel is built
 // around keeping HBM busy:
-//  * Persistent CTAs (one per SM) deal out (row, kv-head group, split) units.
-//    A unit covers HB = up to 4 KV heads of one row: a selected token's K||V
+//  * Persistent CTAs (one per SM) take contiguous ranges of the (row,
+//    kv-head group, token tile) work (stream-K), so a row is met by only a
+//    few CTAs, each writing one partial of it.  A pair covers HB = up to 4
+//    KV heads of one row: a selected token's K||V
 //    rows of those heads are one contiguous run (2 KB at head_dim 128), moved
 //    by ONE bulk copy (cp.async.bulk on the TMA engine) into a 4-stage
 //    shared-memory ring guarded by mbarriers.  Token rows are padded by 16 B
@@ -78,20 +80,43 @@ struct Unit {
   int row, hg, split, t0, t1, n_cols;
 };
 
+// Stream-K split: CTA c owns units [U*c/C, U*(c+1)/C) of the U = pairs x
+// pair_tiles work units (pair = (row, kv-head group), pairs in row-major order).
+__device__ __forceinline__ int64_t sk_begin(const AttnParams& p, int c) {
+  return p.sk_units * c / p.sk_ctas;
+}
+// The CTA whose range holds unit x: the largest c with U*c/C <= x.
+__device__ __forceinline__ int sk_owner(const AttnParams& p, int64_t x) {
+  return static_cast<int>(((x + 1) * p.sk_ctas + p.sk_units - 1) / p.sk_units - 1);
+}
+
+// The k-th pair this CTA meets, its tile range inside the pair (clipped to
+// the row's valid tiles; may be empty) and its partial slot index.
 template <int TT>
-__device__ __forceinline__ Unit decode_unit(const AttnParams& p, int u, int groups) {
+__device__ __forceinline__ Unit unit_of(const AttnParams& p, int groups, int64_t ua, int64_t ub,
+                                        int k) {
   Unit x;
-  x.split = u % p.splits;
-  const int rest = u / p.splits;
-  x.hg = rest % groups;
-  x.row = rest / groups;
+  const int T = p.pair_tiles;
+  const int64_t g = ua / T + k;
+  x.hg = static_cast<int>(g % groups);
+  x.row = static_cast<int>(g / groups);
   int n = p.topk_width;
   if (p.valid_counts != nullptr) n = min(max(p.valid_counts[x.row], 0), p.topk_width);
   x.n_cols = n;
   const int tiles = (n + TT - 1) / TT;
-  x.t0 = x.split * tiles / p.splits;
-  x.t1 = (x.split + 1) * tiles / p.splits;
+  const int64_t first = g * T;
+  const int t0 = static_cast<int>(max(ua, first) - first);
+  const int t1 = static_cast<int>(min(ub, first + T) - first);
+  x.t1 = min(t1, tiles);
+  x.t0 = min(t0, x.t1);
+  x.split = static_cast<int>(blockIdx.x) - sk_owner(p, first);
   return x;
+}
+
+// Pairs met by this CTA's range [ua, ub).
+__device__ __forceinline__ int units_met(const AttnParams& p, int64_t ua, int64_t ub) {
+  if (ub <= ua) return 0;
+  return static_cast<int>((ub - 1) / p.pair_tiles - ua / p.pair_tiles + 1);
 }
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
@@ -104,26 +129,29 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid
 // prefetch token ids ahead of the copies.
 template <int TT>
 struct Cursor {
-  int u, t, units, groups;
+  int k, t, units, groups;
+  int64_t ua, ub;
   Unit x;
   bool live;
-  __device__ void init(const AttnParams& p, int units_, int groups_) {
+  __device__ void init(const AttnParams& p, int units_, int groups_, int64_t ua_, int64_t ub_) {
     units = units_;
     groups = groups_;
-    u = blockIdx.x;
-    live = u < units;
+    ua = ua_;
+    ub = ub_;
+    k = 0;
+    live = k < units;
     if (live) {
-      x = decode_unit<TT>(p, u, groups);
+      x = unit_of<TT>(p, groups, ua, ub, k);
       t = x.t0;
       skip(p);
     }
   }
   __device__ void skip(const AttnParams& p) {
     while (live && t >= x.t1) {
-      u += gridDim.x;
-      live = u < units;
+      ++k;
+      live = k < units;
       if (live) {
-        x = decode_unit<TT>(p, u, groups);
+        x = unit_of<TT>(p, groups, ua, ub, k);
         t = x.t0;
       }
     }
@@ -135,7 +163,8 @@ struct Cursor {
 };
 
 template <int D, int NT, int HB>
-__device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups) {
+__device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups,
+                         int64_t ua, int64_t ub) {
   using S = Smem<D, NT, HB>;
   constexpr int kRow = S::kRow;
   constexpr int TT = S::kTT;
@@ -148,7 +177,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   int32_t (*ring)[64] = sm.ring[pw];
 
   Cursor<TT> ahead;  // this producer's own tiles: positions pw, pw + kProducers, ...
-  ahead.init(p, units, groups);
+  ahead.init(p, units, groups, ua, ub);
   for (int i = 0; i < pw; ++i) ahead.next(p);
   auto prefetch = [&](int slot) {
     if (ahead.live) {
@@ -167,8 +196,8 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 
   int it = 0, k = 0, own = 0;
   bool ok = true;
-  for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++k) {
-    const Unit x = decode_unit<TT>(p, u, groups);
+  for (; k < units && ok; ++k) {
+    const Unit x = unit_of<TT>(p, groups, ua, ub, k);
     // ---- the unit's query rows -> q[k & 1] (producer 0 only)
     const int qb = k & 1;
     if (pw == 0 && k >= 2 && !mbar_wait(&sm.qempty[qb], ((k >> 1) - 1) & 1)) {
@@ -317,7 +346,8 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 }
 
 template <int D, int NT, int HB>
-__device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups) {
+__device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups,
+                         int64_t ua, int64_t ub) {
   using S = Smem<D, NT, HB>;
   constexpr int TT = S::kTT;
   constexpr int SUB = kGroupWarps / HB;  // 16-token sub-tiles per stage per head
@@ -349,8 +379,8 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   // reaches every named barrier, so no warp of the CTA is left waiting at one.
   bool aborted = false;
   int it = 0, k = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x, ++k) {
-    const Unit x = decode_unit<TT>(p, u, groups);
+  for (; k < units; ++k) {
+    const Unit x = unit_of<TT>(p, groups, ua, ub, k);
     const int qb = k & 1;
     aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
     if (!aborted && !mbar_wait(&sm.qfull[qb], (k >> 1) & 1)) {
@@ -499,7 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem<D, NT, HB>& sm = *reinterpret_cast<Smem<D, NT, HB>*>(smem_raw);
   const int groups = p.kv_heads / HB;
-  const int units = p.rows * groups * p.splits;
+  const int64_t ua = sk_begin(p, blockIdx.x), ub = sk_begin(p, blockIdx.x + 1);
+  const int units = units_met(p, ua, ub);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 32);
@@ -514,9 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
   }
   __syncthreads();
   if (threadIdx.x >= kConsumerWarps * 32)
-    producer<D, NT, HB>(p, sm, units, groups);
+    producer<D, NT, HB>(p, sm, units, groups, ua, ub);
   else
-    consumer<D, NT, HB>(p, sm, units, groups);
+    consumer<D, NT, HB>(p, sm, units, groups, ua, ub);
 }
 
 // Merge of the partial (normalized O, LSE) slots of every (row, query head):
@@ -534,7 +565,11 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
   const int d0 = (threadIdx.x & 31) * DPL;
   const int64_t slot_stride = static_cast<int64_t>(p.rows) * p.q_heads;
   const int64_t base = static_cast<int64_t>(row) * p.q_heads + head;
-  const int P = p.partials;
+  // partial slots of this head: slot_group per CTA whose range met its pair
+  const int groups = p.kv_heads / p.heads_per_unit;
+  const int hg = (head / (p.q_heads / p.kv_heads)) / p.heads_per_unit;
+  const int64_t first = (static_cast<int64_t>(row) * groups + hg) * p.pair_tiles;
+  const int P = (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) * p.slot_group;
   const int lane = threadIdx.x & 31;
   // max LSE: the warp's lanes load 32 slots at a time
   float M = -INFINITY;
@@ -605,8 +640,7 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const int units = p.rows * (p.kv_heads / HB) * p.splits;
-  const int grid = std::min(units, num_sms());
+  const int grid = p.sk_ctas;
   attention_kernel<D, NT, HB><<<grid, kThreads, smem, stream>>>(p);
   e = count_launches(cudaGetLastError());
   if (e != cudaSuccess) return e;
@@ -639,45 +673,29 @@ int attention_heads_per_unit(int q_heads, int kv_heads) {
   return 1;
 }
 
-// Split count for `base` units of `tiles` tiles on a persistent grid of G
-// CTAs that deals units round-robin: simulate the deal for each split count
-// and keep the one whose busiest CTA walks the fewest tiles (a unit's start
-// and epilogue ~ one tile; more partials make the merge ~ 1/8 tile each).
-int best_split(int base, int tiles, int G) {
-  int best = 1;
-  double best_cost = 1e30;
-  const int max_split = std::min(tiles, 32);
-  for (int S = 1; S <= max_split; ++S) {
-    const int units = base * S;
-    double worst = 0.0;
-    for (int c = 0; c < std::min(units, G); ++c) {
-      double load = 0.0;
-      for (int u = c; u < units; u += G) {
-        const int sp = u % S;
-        load += ((sp + 1) * tiles / S - sp * tiles / S) + 1.0;
-      }
-      worst = std::max(worst, load);
-    }
-    const double cost = worst + 0.125 * S;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = S;
-    }
-  }
-  return best;
-}
-
+// Stream-K plan: U = pairs x pair_tiles units cut into one contiguous range
+// per CTA (one CTA per SM, or one per unit when there are fewer).  The
+// workspace holds, per (row, head), slot_group partial slots for each CTA that
+// can meet one pair: the largest such count over the pairs, computed with the
+// same integer arithmetic as the kernels.
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
                         int use_decode_kernel) {
   (void)use_decode_kernel;
-  AttnPlan plan{1, 0, 0};
+  AttnPlan plan{};
   const int hb = attention_heads_per_unit(q_heads, kv_heads);
   const int tt = 64 / hb;
-  const int base = rows * (kv_heads / hb);
-  const int tiles = (topk_width + tt - 1) / tt;
-  const int G = num_sms();
-  if (base > 0 && tiles > 1 && base < 4 * G) plan.splits = best_split(base, tiles, G);
-  plan.partials = plan.splits * kGroups * (kGroupWarps / hb);
+  const int64_t pairs = static_cast<int64_t>(rows) * (kv_heads / hb);
+  plan.heads_per_unit = hb;
+  plan.slot_group = kGroups * (kGroupWarps / hb);
+  plan.pair_tiles = std::max(1, (topk_width + tt - 1) / tt);
+  plan.units = pairs * plan.pair_tiles;
+  plan.ctas = static_cast<int>(std::min<int64_t>(plan.units, num_sms()));
+  if (plan.units <= 0) return plan;
+  const int64_t U = plan.units, C = plan.ctas, T = plan.pair_tiles;
+  auto owner = [&](int64_t x) { return ((x + 1) * C + U - 1) / U - 1; };
+  int64_t most = 1;
+  for (int64_t g = 0; g < pairs; ++g) most = std::max(most, owner(g * T + T - 1) - owner(g * T) + 1);
+  plan.partials = static_cast<int>(most) * plan.slot_group;
   const size_t o_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * dim * sizeof(float);
   const size_t l_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * sizeof(float);
   plan.workspace_bytes = ((o_bytes + 255) & ~static_cast<size_t>(255)) + l_bytes;

@@ -438,7 +438,11 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.kv_fused = fused ? (k_head_stride == 2 * head_dim ? 2 : 1) : 0;
   p.slot_contig = k_block_stride == static_cast<int64_t>(page_size) * k_token_stride &&
                   k_token_stride == static_cast<int64_t>(num_kv_heads) * k_head_stride;
-  p.splits = plan.splits;
+  p.pair_tiles = plan.pair_tiles;
+  p.sk_ctas = plan.ctas;
+  p.sk_units = plan.units;
+  p.slot_group = plan.slot_group;
+  p.heads_per_unit = plan.heads_per_unit;
   p.partials = plan.partials;
   {
     const size_t o_bytes =

@@ -100,15 +100,27 @@ struct AttnParams {
   int physical;
   int kv_fused;     // 2: K||V of consecutive heads contiguous; 1: per head; 0: apart
   int slot_contig;  // consecutive slots are adjacent in memory (block stride = page * token stride)
-  int splits;       // split-K factor per (row, kv-head group)
-  int partials;     // partial (O, LSE) slots per (row, head) the merge combines
+  // Stream-K work split: the (row, kv-head group) pairs x pair_tiles token
+  // tiles form sk_units units of work, cut into sk_ctas contiguous ranges
+  // (one per CTA).  A pair's partial results come from the CTAs whose ranges
+  // meet it: slot_group partial slots per CTA (consumer groups x sub-tiles).
+  int pair_tiles;       // token tiles per pair (upper bound: topk_width / tile)
+  int sk_ctas;          // CTAs of the main kernel
+  int64_t sk_units;     // pairs * pair_tiles
+  int slot_group;       // partial slots one CTA writes per (row, head) it meets
+  int heads_per_unit;   // KV heads per pair
+  int partials;         // partial (O, LSE) slots per (row, head) in the workspace
   float* part_o;    // [partials, rows, q_heads, dim] fp32
   float* part_lse;  // [partials, rows, q_heads] fp32
   int* err;
 };
 struct AttnPlan {
-  int splits;
-  int partials;
+  int pair_tiles;     // token tiles per (row, kv-head group) pair
+  int ctas;           // main-kernel CTAs (contiguous unit ranges)
+  int64_t units;      // pairs * pair_tiles
+  int slot_group;     // partial slots per CTA met, per (row, head)
+  int heads_per_unit; // KV heads per pair
+  int partials;       // partial slots per (row, head): most CTAs any pair meets * slot_group
   size_t workspace_bytes;
 };
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,

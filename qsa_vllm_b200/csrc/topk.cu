@@ -10,10 +10,15 @@
 //   * one CTA of 512 threads per row slice; each thread keeps its keys (16,
 //     or 64 for very wide rows) in REGISTERS after one coalesced 16-byte load
 //     pass from HBM, so every radix pass re-reads registers, not memory;
-//   * radix select, most-significant digit first, 11/11/10-bit digits, with
-//     warp-aggregated shared-memory histograms (double-buffered, so a pass
-//     needs a single barrier); a pass stops early once the threshold digit's
-//     bucket is taken whole;
+//   * radix select, most-significant digit first, in digits of up to 11
+//     bits below the high bits shared by every key of the row (found from the
+//     row's min and max key first: scores of similar magnitude share sign and
+//     exponent bits, which would otherwise crowd a few histogram bins), with
+//     shared-memory histograms (double-buffered, so a pass needs a single
+//     barrier); a pass stops early once the threshold digit's bucket is taken
+//     whole;
+//   * the ordered write-out ranks every selected key with ONE block scan of
+//     per-chunk (above, tied) counters;
 //   * rows wider than one CTA's slice run as a thread-block CLUSTER: the
 //     per-CTA histograms are summed through distributed shared memory (DSMEM)
 //     and every CTA derives the same threshold; tied keys are then taken in
@@ -126,13 +131,55 @@ __device__ __forceinline__ void finish_row(const TopkParams& p, const RowMeta& m
     p.counts[row] = min(expanded + m.tail_count, m.seq);
 }
 
-// Warp-aggregated shared-memory histogram increment (all 32 lanes call it).
+// Shared-memory histogram increment.  The digits lie below the row's common
+// high bits, so lanes rarely collide on a bin.
 __device__ __forceinline__ void hist_add(int* hist, bool valid, uint32_t bin) {
-  if (!__any_sync(0xffffffffu, valid)) return;
-  const uint32_t key = valid ? bin : 0xffffffffu;
-  const unsigned peers = __match_any_sync(0xffffffffu, key);
-  if (valid && (threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1))
-    atomicAdd(hist + bin, __popc(peers));
+  if (valid) atomicAdd(hist + bin, 1);
+}
+
+// Block-wide exclusive prefix sums of NC counters per thread in one round
+// (one barrier pair): ex[c] = sum of v[c] over lower threads, tot[c] = sum
+// over the block.  `tmp` holds kWarps * NC ints.
+template <int NC>
+__device__ __forceinline__ void block_scan_multi(const int (&v)[NC], int (&ex)[NC],
+                                                 int (&tot)[NC], int* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) x[c] = v[c];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int y = __shfl_up_sync(0xffffffffu, x[c], o);
+      if (lane >= o) x[c] += y;
+    }
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) tmp[warp * NC + c] = x[c];
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      int w = lane < kWarps ? tmp[lane * NC + c] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      __syncwarp();
+      if (lane < kWarps) tmp[lane * NC + c] = w;  // inclusive warp prefix
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    tot[c] = tmp[(kWarps - 1) * NC + c];
+    ex[c] = (warp == 0 ? 0 : tmp[(warp - 1) * NC + c]) + x[c] - v[c];
+  }
+  __syncthreads();
 }
 
 // Block-wide exclusive prefix sum of one int per thread; also returns the total.
@@ -171,7 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   constexpr int kChunkKeys = 4 * kThreads;
   extern __shared__ int sel[];  // selected column ids of this CTA, by rank (topk entries)
   __shared__ int hist[2][kBins];
-  __shared__ int warp_tmp[kWarps];
+  __shared__ int warp_tmp[kWarps * kChunks * 2];
+  __shared__ uint32_t s_minmax[2][kWarps];
+  __shared__ uint32_t s_range[2];  // this CTA's (min, max) key
   __shared__ int s_bin, s_remaining, s_bin_count;
   __shared__ int s_counts[2];  // (strictly above, tied) in this CTA's slice
 
@@ -217,57 +266,97 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     }
   }
   auto valid_at = [&](int i) { return 4 * ((i / 4) * kThreads + tid) + (i % 4) < n; };
-  const int chunks_used = (n + kChunkKeys - 1) / kChunkKeys;
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < V; ++i) hist_add(hist[0], valid_at(i), key[i] >> 21);
 
-  // ---- radix passes: digits of 11, 11, 10 bits from the most significant.
-  uint32_t prefix = 0;  // resolved high bits: the threshold is (key >> shift) == prefix
-  int shift = 32;
+  // ---- min and max key of the row: their common high bits are shared by
+  // every key and need no radix pass.
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    if (valid_at(i)) {
+      kmin = min(kmin, key[i]);
+      kmax = max(kmax, key[i]);
+    }
+  }
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  if ((tid & 31) == 0) {
+    s_minmax[0][tid >> 5] = kmin;
+    s_minmax[1][tid >> 5] = kmax;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t a = tid < kWarps ? s_minmax[0][tid] : 0xffffffffu;
+    uint32_t z = tid < kWarps ? s_minmax[1][tid] : 0u;
+    a = __reduce_min_sync(0xffffffffu, a);
+    z = __reduce_max_sync(0xffffffffu, z);
+    if (tid == 0) {
+      s_range[0] = a;
+      s_range[1] = z;
+    }
+  }
+  __syncthreads();
+  kmin = s_range[0];
+  kmax = s_range[1];
+  if (C > 1) {
+    cluster.sync();  // every CTA's (min, max) published
+    for (int r = 0; r < C; ++r) {
+      const uint32_t* rr = cluster.map_shared_rank(&s_range[0], r);
+      kmin = min(kmin, rr[0]);
+      kmax = max(kmax, rr[1]);
+    }
+  }
+  const int common = kmin == kmax ? 32 : __clz(kmin ^ kmax);  // shared high bits
+
+  // ---- radix passes over the bits below the common prefix, digits of <= 11.
+  int shift = 32 - common;
+  uint32_t prefix = common == 0 ? 0u : kmax >> shift;  // resolved high bits of the threshold
   int remaining = topk;  // how many of the keys matching `prefix` are still to be taken
-  for (int pass = 0;; ++pass) {
+  for (int pass = 0; shift > 0; ++pass) {
     const int b = pass & 1;
-    const int dbits = pass < 2 ? 11 : 10;
+    const int dbits = shift < 11 ? shift : 11;
     const int dshift = shift - dbits;
     const uint32_t dmask = (1u << dbits) - 1u;
-    if (pass > 0) {
-      if (pass >= 2) {  // hist[b] was last read by the cluster two passes ago
-        for (int i = tid; i < kBins; i += kThreads) hist[b][i] = 0;
-        __syncthreads();
-      }
+    if (pass >= 2) {  // hist[b] was last read (cluster-wide) two passes ago
+      for (int i = tid; i < kBins; i += kThreads) hist[b][i] = 0;
+      __syncthreads();
+    }
 #pragma unroll
-      for (int i = 0; i < V; ++i)
-        hist_add(hist[b], valid_at(i) && (key[i] >> shift) == prefix, (key[i] >> dshift) & dmask);
+    for (int i = 0; i < V; ++i) {
+      const bool in = valid_at(i) && (shift >= 32 || (key[i] >> shift) == prefix);
+      hist_add(hist[b], in, (key[i] >> dshift) & dmask);
     }
     __syncthreads();
     if (C > 1) cluster.sync();  // every CTA's histogram of this pass is complete
 
-    // Thread t owns the 4 bins just below the 4t highest (descending order).
+    // Thread t owns per_thread bins just below the per_thread*t highest
+    // (descending order); with fewer bins than threads, one bin each.
     const int nb = 1 << dbits;
-    const int per_thread = nb / kThreads;  // 4 or 2
+    const int per_thread = nb >= kThreads ? nb / kThreads : 1;  // 4, 2 or 1
+    const bool owns = per_thread * tid < nb;
     const int top = nb - 1 - per_thread * tid;
     int h[4] = {0, 0, 0, 0};
-    if (C > 1) {
+    if (owns) {
+      if (C > 1) {
 #pragma unroll
-      for (int r = 0; r < kMaxCluster; ++r) {
-        if (r < C) {
-          const int* rh = cluster.map_shared_rank(&hist[b][0], r);
+        for (int r = 0; r < kMaxCluster; ++r) {
+          if (r < C) {
+            const int* rh = cluster.map_shared_rank(&hist[b][0], r);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (j < per_thread) h[j] += rh[top - j];
+            for (int j = 0; j < 4; ++j)
+              if (j < per_thread) h[j] += rh[top - j];
+          }
         }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (j < per_thread) h[j] = hist[b][top - j];
+        for (int j = 0; j < 4; ++j)
+          if (j < per_thread) h[j] = hist[b][top - j];
+      }
     }
     int total;
     int above = block_exclusive_sum(h[0] + h[1] + h[2] + h[3], warp_tmp, total);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (j < per_thread && above < remaining && remaining <= above + h[j]) {
+      if (owns && j < per_thread && above < remaining && remaining <= above + h[j]) {
         s_bin = top - j;
         s_remaining = remaining - above;
         s_bin_count = h[j];
@@ -275,25 +364,38 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
       above += h[j];
     }
     __syncthreads();
-    prefix = (prefix << dbits) | static_cast<uint32_t>(s_bin);
+    prefix = (shift >= 32 ? 0u : (prefix << dbits)) | static_cast<uint32_t>(s_bin);
     remaining = s_remaining;
     shift = dshift;
-    const bool done = s_bin_count == remaining || shift == 0;
+    const bool done = s_bin_count == remaining;
     __syncthreads();  // s_* are rewritten by the next pass
     if (done) break;
   }
 
   // ---- ordered write-out.  strict: (key >> shift) > prefix; tie: == prefix.
-  int my_strict = 0, my_tie = 0;
+  // (shift < 32 here: at least the sign bit was resolved or shared.)
+  // Counters per chunk c, packed (strict << 16 | tie); one block scan ranks
+  // every key of the CTA's slice in column order.
+  int cnt[kChunks], ex[kChunks], tot[kChunks];
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const uint32_t d = key[i] >> shift;
-    my_strict += valid_at(i) && d > prefix;
-    my_tie += valid_at(i) && d == prefix;
+  for (int c = 0; c < kChunks; ++c) {
+    int fs = 0, ft = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t d = key[4 * c + j] >> shift;
+      const bool v = valid_at(4 * c + j);
+      fs += v && d > prefix;
+      ft += v && d == prefix;
+    }
+    cnt[c] = (fs << 16) | ft;
   }
-  int tot_strict, tot_tie;  // up to 32768 each: two sums, no 16-bit packing
-  block_exclusive_sum(my_strict, warp_tmp, tot_strict);
-  block_exclusive_sum(my_tie, warp_tmp, tot_tie);
+  block_scan_multi<kChunks>(cnt, ex, tot, warp_tmp);
+  int tot_strict = 0, tot_tie = 0;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    tot_strict += tot[c] >> 16;
+    tot_tie += tot[c] & 0xffff;
+  }
   int base_rank = 0, ties_before = 0;
   if (C > 1) {
     if (tid == 0) {
@@ -315,19 +417,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   int run_strict = 0, run_tie = 0;
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
-    if (c >= chunks_used) break;  // uniform across the CTA
-    int fs = 0, ft = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t d = key[4 * c + j] >> shift;
-      const bool v = valid_at(4 * c + j);
-      fs += v && d > prefix;
-      ft += v && d == prefix;
-    }
-    int round_total;
-    const int ex = block_exclusive_sum((fs << 16) | ft, warp_tmp, round_total);
-    int sb = run_strict + (ex >> 16);
-    int tb = run_tie + (ex & 0xffff);
+    int sb = run_strict + (ex[c] >> 16);
+    int tb = run_tie + (ex[c] & 0xffff);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t d = key[4 * c + j] >> shift;
@@ -341,8 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
         ++tb;
       }
     }
-    run_strict += round_total >> 16;
-    run_tie += round_total & 0xffff;
+    run_strict += tot[c] >> 16;
+    run_tie += tot[c] & 0xffff;
   }
   __syncthreads();
   // Expansion: one rank per thread and iteration, so consecutive threads
