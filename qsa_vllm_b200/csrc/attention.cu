@@ -544,6 +544,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x >= kConsumerWarps * 32)
     producer<D, NT, HB>(p, sm, units, groups, ua, ub);
   else
@@ -558,6 +560,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
 constexpr int kMergeHeads = 8;
 template <int D>
 __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int DPL = D / 32;  // dims per lane
   const int row = blockIdx.x;
   const int head = blockIdx.y * kMergeHeads + (threadIdx.x >> 5);
@@ -641,12 +645,12 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
                                 static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int grid = p.sk_ctas;
-  attention_kernel<D, NT, HB><<<grid, kThreads, smem, stream>>>(p);
-  e = count_launches(cudaGetLastError());
+  e = count_launches(
+      launch_kernel(attention_kernel<D, NT, HB>, dim3(grid), dim3(kThreads), smem, stream, 1, p));
   if (e != cudaSuccess) return e;
-  merge_kernel<D><<<dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads), kMergeHeads * 32,
-                     0, stream>>>(p);
-  return count_launches(cudaGetLastError());
+  return count_launches(launch_kernel(
+      merge_kernel<D>, dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads),
+      dim3(kMergeHeads * 32), 0, stream, 1, p));
 }
 
 template <int D, int NT>

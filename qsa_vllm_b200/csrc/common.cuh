@@ -7,6 +7,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
+
 namespace qsa {
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
@@ -181,5 +184,55 @@ struct FastDiv {
     r = n - q * static_cast<int>(d);
   }
 };
+
+// ------------------------------------------- programmatic dependent launch
+// Every kernel of this library waits for the grids it depends on (the
+// preceding kernels of its stream) before its first global memory access, and
+// lets its own dependents launch right after.  Launched with programmatic
+// stream serialization, a kernel's launch and prologue (barrier set-up, TMEM
+// allocation, tensor-map prefetch) then overlap the tail of the kernel before
+// it; launched without it, the wait returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// QSA_PDL=0 launches every kernel with plain stream order.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("QSA_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization (when enabled)
+// plus an optional cluster shape.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace qsa

@@ -48,6 +48,8 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 template <int D, int NT>
 __global__ void __launch_bounds__(kThreads) indexer_kernel(const IndexerParams p, int rows_per_cta,
                                                            int keys_per_cta) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   auto& sm = *reinterpret_cast<IdxSmem<D, NT>*>(smem_raw);
   constexpr int CPR = D / 8;  // 16-byte chunks per key row
@@ -236,8 +238,8 @@ cudaError_t launch_dn(const IndexerParams& p, dim3 grid, int rows_per_cta, int k
   cudaError_t e = set_attr_once(reinterpret_cast<const void*>(indexer_kernel<D, NT>), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  indexer_kernel<D, NT><<<grid, kThreads, smem, stream>>>(p, rows_per_cta, keys_per_cta);
-  return count_launches(cudaGetLastError());
+  return count_launches(launch_kernel(indexer_kernel<D, NT>, grid, dim3(kThreads), smem, stream,
+                                      1, p, rows_per_cta, keys_per_cta));
 }
 
 template <int D>
@@ -308,6 +310,8 @@ __device__ __forceinline__ long long floor_div(long long a, long long b) {
 __global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* seq_lens,
                                       int num_requests, const int32_t* token_to_req, int rows,
                                       int ratio, int32_t* visible) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const int req = token_to_req[r];
@@ -325,8 +329,8 @@ cudaError_t launch_visible_blocks(const int64_t* positions, const int32_t* seq_l
                                   int num_requests, const int32_t* token_to_req, int rows,
                                   int ratio, int32_t* visible, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  visible_blocks_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(
-      positions, seq_lens, num_requests, token_to_req, rows, ratio, visible);
-  return count_launches(cudaGetLastError());
+  return count_launches(launch_kernel(visible_blocks_kernel, dim3((rows + 255) / 256), dim3(256),
+                                      0, stream, 1, positions, seq_lens, num_requests,
+                                      token_to_req, rows, ratio, visible));
 }
 }  // namespace qsa

@@ -332,6 +332,8 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ================================================================ producer
@@ -673,9 +675,8 @@ cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& kmap, const CUt
   if (e != cudaSuccess) return e;
   per_sm = std::max(1, std::min(per_sm, 512 / C::kCols));  // resident CTAs share 512 columns
   const int64_t ctas = std::min<int64_t>(g.units, static_cast<int64_t>(num_sms()) * per_sm);
-  indexer_tc_kernel<D, NQ><<<static_cast<int>(ctas), kTcThreads, smem, stream>>>(kmap, qmap, p,
-                                                                                  g);
-  return count_launches(cudaGetLastError());
+  return count_launches(launch_kernel(indexer_tc_kernel<D, NQ>, dim3(static_cast<int>(ctas)),
+                                      dim3(kTcThreads), smem, stream, 1, kmap, qmap, p, g));
 }
 
 }  // namespace

@@ -224,6 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   __shared__ int s_bin, s_remaining, s_bin_count;
   __shared__ int s_counts[2];  // (strictly above, tied) in this CTA's slice
 
+  pdl_wait();
+  pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int crank = static_cast<int>(cluster.block_rank());
@@ -466,19 +468,10 @@ cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(std::max(p.topk, 1)) * sizeof(int);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return count_launches(cudaLaunchKernelEx(&cfg, topk_kernel<V>, p));
+  return count_launches(launch_kernel(
+      topk_kernel<V>, dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows)),
+      dim3(kThreads), static_cast<size_t>(std::max(p.topk, 1)) * sizeof(int), stream,
+      static_cast<unsigned>(C), p));
 }
 
 }  // namespace
