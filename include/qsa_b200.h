@@ -85,6 +85,9 @@ enum { QSA_DEVICE_ERR_WAIT_TIMEOUT = 1 };
  * scores: fp32 [rows, score_width] (unit column stride).
  * positions: int64 [rows]; sequence_lengths: int32 [num_requests];
  * token_to_req, lengths: int32 [rows]; output: int32 [rows, output_width].
+ * lengths may be NULL: each row's length is then its visible block count
+ * min((positions[r] + 1) // ratio, sequence_lengths[req] // ratio) (0 for an
+ * unmapped row), as qsa_visible_blocks computes it.
  */
 QSA_API int qsa_topk_expand(const float* scores, int64_t score_row_stride, int32_t rows,
                     int32_t score_width, const int32_t* lengths, const int64_t* positions,
@@ -123,13 +126,20 @@ QSA_API int qsa_topk(const float* scores, int64_t score_row_stride, int32_t rows
  * [num_blocks, page_size, 1, head_dim] (unit dim stride); weights: fp32
  * [rows, num_heads] or NULL for all ones (the reference's weighting);
  * reference scale = head_dim ** -0.5.  head_dim must be 64 or 128.
+ * visible may be NULL: row r's count is then derived as qsa_visible_blocks
+ * does from positions (int64, indexed like visible), sequence_lengths
+ * [num_sequences] and token_to_req (indexed like visible) with `ratio`; these
+ * four are ignored when visible is given.
  */
 QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                        int32_t num_heads, int32_t head_dim, const void* k_cache,
                        int64_t cache_block_stride, int64_t cache_token_stride,
                        int32_t num_blocks, int32_t page_size, const int32_t* page_table,
                        int64_t table_row_stride, int32_t table_width, int32_t num_requests,
-                       const int32_t* visible, const int32_t* query_start_loc,
+                       const int32_t* visible, const int64_t* positions,
+                       const int32_t* sequence_lengths, int32_t num_sequences,
+                       const int32_t* token_to_req, int32_t ratio,
+                       const int32_t* query_start_loc,
                        int32_t decode_query_len, int32_t max_query_len, int32_t query_offset,
                        int32_t num_rows, const float* weights, int64_t weight_row_stride,
                        int64_t weight_head_stride, float scale, float* logits,

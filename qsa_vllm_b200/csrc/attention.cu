@@ -575,63 +575,71 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
   const int64_t first = (static_cast<int64_t>(row) * groups + hg) * p.pair_tiles;
   const int P = (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) * p.slot_group;
   const int lane = threadIdx.x & 31;
-  // max LSE: the warp's lanes load 32 slots at a time
-  float M = -INFINITY;
-  for (int s0 = 0; s0 < P; s0 += 32)
-    if (s0 + lane < P) M = fmaxf(M, __ldg(p.part_lse + (s0 + lane) * slot_stride + base));
+  // the gate does not depend on the partials: its loads go out first
+  float gv[DPL];
+  const __nv_bfloat16* gp = p.gate == nullptr ? nullptr
+                            : static_cast<const __nv_bfloat16*>(p.gate) +
+                                  static_cast<int64_t>(row) * p.gate_row_stride +
+                                  static_cast<int64_t>(head) * p.gate_head_stride;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  for (int i = 0; i < DPL; ++i)
+    gv[i] = gp != nullptr ? __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride])
+                          : 0.f;
   float den = 0.f;
   float acc[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  if (M > -INFINITY) {
-    // 8 slots per batch: all 16 loads are issued before any is used
-    for (int s0 = 0; s0 < P; s0 += 8) {
-      float lse[8];
-      float v[8][DPL];
+  // 8 slots per batch: every slot's LSE and partial are loaded before any is
+  // used; with at most 8 slots (the common case) that is the only round trip.
+  float M = -INFINITY;
+  for (int s0 = 0; s0 < P; s0 += 8) {
+    float lse[8];
+    float v[8][DPL];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t b = (s0 + j < P ? s0 + j : 0) * slot_stride + base;
-        lse[j] = s0 + j < P ? __ldg(p.part_lse + b) : -INFINITY;
-        const float* po = p.part_o + b * D + d0;
-        if constexpr (DPL == 4) {
-          const float4 t = __ldg(reinterpret_cast<const float4*>(po));
-          v[j][0] = t.x;
-          v[j][1] = t.y;
-          v[j][2] = t.z;
-          v[j][3] = t.w;
-        } else {
-          const float2 t = __ldg(reinterpret_cast<const float2*>(po));
-          v[j][0] = t.x;
-          v[j][1] = t.y;
-        }
+    for (int j = 0; j < 8; ++j) {
+      const int64_t b = (s0 + j < P ? s0 + j : 0) * slot_stride + base;
+      lse[j] = s0 + j < P ? __ldg(p.part_lse + b) : -INFINITY;
+      const float* po = p.part_o + b * D + d0;
+      if constexpr (DPL == 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(po));
+        v[j][0] = t.x;
+        v[j][1] = t.y;
+        v[j][2] = t.z;
+        v[j][3] = t.w;
+      } else {
+        const float2 t = __ldg(reinterpret_cast<const float2*>(po));
+        v[j][0] = t.x;
+        v[j][1] = t.y;
       }
+    }
+    float m_new = M;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float w = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
-        den += w;
+    for (int j = 0; j < 8; ++j) m_new = fmaxf(m_new, lse[j]);
+    if (m_new == -INFINITY) continue;  // no valid slot yet
+    // rescale what earlier batches accumulated to the new maximum
+    const float r = M == -INFINITY ? 0.f : exp2f(M - m_new);
+    den *= r;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * w;
-      }
+    for (int i = 0; i < DPL; ++i) acc[i] *= r;
+    M = m_new;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float w = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
+      den += w;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * w;
     }
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
                       static_cast<int64_t>(row) * p.out_row_stride +
                       static_cast<int64_t>(head) * p.out_head_stride + d0;
-  const __nv_bfloat16* gp = p.gate == nullptr ? nullptr
-                            : static_cast<const __nv_bfloat16*>(p.gate) +
-                                  static_cast<int64_t>(row) * p.gate_row_stride +
-                                  static_cast<int64_t>(head) * p.gate_head_stride;
 #pragma unroll
   for (int i = 0; i < DPL; i += 2) {
     float o0 = acc[i] * inv, o1 = acc[i + 1] * inv;
     if (gp != nullptr) {
-      const float g0 = __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride]);
-      const float g1 = __bfloat162float(gp[static_cast<int64_t>(d0 + i + 1) * p.gate_dim_stride]);
-      o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-g0));
-      o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-g1));
+      o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-gv[i]));
+      o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-gv[i + 1]));
     }
     *reinterpret_cast<__nv_bfloat162*>(op + i) = __floats2bfloat162_rn(o0, o1);
   }

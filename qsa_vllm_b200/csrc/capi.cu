@@ -165,7 +165,8 @@ int qsa_device_error_poll(int32_t* error_bits) {
 static int topk_common(TopkParams& p, void* stream, const char* who) {
   if (p.rows < 0 || p.width < 0) return fail(QSA_ERR_INVALID, "%s: negative rows/width", who);
   if (p.rows == 0) return QSA_OK;
-  if (!p.scores || !p.lengths || !p.output)
+  // lengths may be NULL only when the kernel can derive them (expansion)
+  if (!p.scores || (!p.lengths && !p.expand) || !p.output)
     return fail(QSA_ERR_INVALID, "%s: null scores/lengths/output", who);
   if (p.score_row_stride < p.width)
     return fail(QSA_ERR_INVALID, "%s: score row stride %lld < width %d", who,
@@ -252,16 +253,24 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
                        int64_t cache_block_stride, int64_t cache_token_stride,
                        int32_t num_blocks, int32_t page_size, const int32_t* page_table,
                        int64_t table_row_stride, int32_t table_width, int32_t num_requests,
-                       const int32_t* visible, const int32_t* query_start_loc,
-                       int32_t decode_query_len, int32_t max_query_len, int32_t query_offset,
+                       const int32_t* visible, const int64_t* positions,
+                       const int32_t* sequence_lengths, int32_t num_sequences,
+                       const int32_t* token_to_req, int32_t ratio,
+                       const int32_t* query_start_loc, int32_t decode_query_len,
+                       int32_t max_query_len, int32_t query_offset,
                        int32_t num_rows, const float* weights, int64_t weight_row_stride,
                        int64_t weight_head_stride, float scale, float* logits,
                        int64_t logits_row_stride, int32_t logits_width, void* stream) {
   const char* who = "qsa_indexer_scores";
   if (num_rows < 0 || logits_width < 0) return fail(QSA_ERR_INVALID, "%s: negative size", who);
   if (num_rows == 0) return QSA_OK;
-  if (!q || !k_cache || !page_table || !visible || !logits)
+  if (!q || !k_cache || !page_table || !logits)
     return fail(QSA_ERR_INVALID, "%s: null pointer", who);
+  if (!visible && (!positions || !sequence_lengths || !token_to_req || ratio <= 0 ||
+                   num_sequences < 0))
+    return fail(QSA_ERR_INVALID,
+                "%s: without visible counts, positions / sequence_lengths / token_to_req and a "
+                "positive ratio are needed", who);
   if (head_dim != 64 && head_dim != 128)
     return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
   const bool pow2 = num_heads > 0 && num_heads <= 8 && (num_heads & (num_heads - 1)) == 0;
@@ -304,6 +313,11 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
   p.table_width = table_width;
   p.num_requests = num_requests;
   p.visible = visible;
+  p.positions = positions;
+  p.seq_lens = sequence_lengths;
+  p.num_sequences = num_sequences;
+  p.token_to_req = token_to_req;
+  p.ratio = ratio;
   p.query_start_loc = query_start_loc;
   p.decode_query_len = decode_query_len;
   p.max_query_len = max_query_len;

@@ -185,6 +185,24 @@ struct FastDiv {
   }
 };
 
+// ------------------------------------------------------ visible block count
+// Python floor division (b > 0).
+__device__ __forceinline__ long long floor_div_ll(long long a, long long b) {
+  const long long q = a / b;
+  return (a % b != 0 && a < 0) ? q - 1 : q;
+}
+// Compressed blocks row r may attend: min((pos + 1) // ratio, seq_len // ratio)
+// for a row mapped to a request, else 0 (reference ops/indexer.py:363-369).
+__device__ __forceinline__ int visible_of(const int64_t* positions, const int32_t* seq_lens,
+                                          int num_sequences, const int32_t* token_to_req,
+                                          int ratio, int r) {
+  const int req = token_to_req[r];
+  if (req < 0 || req >= num_sequences) return 0;
+  const long long a = floor_div_ll(positions[r] + 1, ratio);
+  const long long b = floor_div_ll(seq_lens[req], ratio);
+  return static_cast<int>(a < b ? a : b);
+}
+
 // ------------------------------------------- programmatic dependent launch
 // Every kernel of this library waits for the grids it depends on (the
 // preceding kernels of its stream) before its first global memory access, and

@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kThreads) indexer_kernel(const IndexerParams p
   const int num_columns = p.table_width * p.page_size;
   const int cap = min(num_columns, p.logits_width);
   int maxvis = 0;
-  for (int i = 0; i < nrows; ++i) maxvis = max(maxvis, min(p.visible[r0 + i], cap));
+  for (int i = 0; i < nrows; ++i) maxvis = max(maxvis, min(row_visible(p, r0 + i), cap));
   const int k0 = blockIdx.z * keys_per_cta;
   const int k1 = min(k0 + keys_per_cta, maxvis);
   if (k0 >= k1) return;
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreads) indexer_kernel(const IndexerParams p
                                             static_cast<int64_t>(h) * p.w_head_stride]
                                : 1.f)
                   : 0.f;
-    sm.limit[tid] = tid < nrows ? min(p.visible[r0 + tid], cap) : 0;
+    sm.limit[tid] = tid < nrows ? min(row_visible(p, r0 + tid), cap) : 0;
   }
 
   // ---- query tile: column n = (row n / H, head n % H)
@@ -301,12 +301,6 @@ cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
 
 namespace qsa {
 namespace {
-// floor division (Python / torch `//` semantics), b > 0
-__device__ __forceinline__ long long floor_div(long long a, long long b) {
-  const long long q = a / b;
-  return (a % b != 0 && a < 0) ? q - 1 : q;
-}
-
 __global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* seq_lens,
                                       int num_requests, const int32_t* token_to_req, int rows,
                                       int ratio, int32_t* visible) {
@@ -314,14 +308,7 @@ __global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* s
   pdl_trigger();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
-  const int req = token_to_req[r];
-  int v = 0;
-  if (req >= 0 && req < num_requests) {
-    const long long a = floor_div(positions[r] + 1, ratio);
-    const long long b = floor_div(seq_lens[req], ratio);
-    v = static_cast<int32_t>(a < b ? a : b);
-  }
-  visible[r] = v;
+  visible[r] = visible_of(positions, seq_lens, num_requests, token_to_req, ratio, r);
 }
 }  // namespace
 

@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
       for (int i = 0; i < (NQ + 31) / 32; ++i) {
         const int n = lane + 32 * i;
         const int ri = n / H, h = n - ri * H;
-        vis_lane[i] = n < nrows ? min(p.visible[r0 + n], cap) : 0;
+        vis_lane[i] = n < nrows ? min(row_visible(p, r0 + n), cap) : 0;
         w_lane[i] = 0.f;
         if (n < NQ && ri < nrows)
           w_lane[i] = p.weights ? p.weights[static_cast<int64_t>(r0 + ri) * p.w_row_stride +

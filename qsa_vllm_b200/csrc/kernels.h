@@ -53,7 +53,11 @@ struct IndexerParams {
   const int32_t* table;
   int64_t table_row_stride;
   int table_width, num_requests;
-  const int32_t* visible;
+  const int32_t* visible;          // nullptr: derived per row from the four fields below
+  const int64_t* positions;        // [rows] (same row indexing as q)
+  const int32_t* seq_lens;         // [num_sequences]
+  const int32_t* token_to_req;     // [rows]
+  int num_sequences, ratio;
   const int32_t* query_start_loc;  // nullptr: uniform decode
   int decode_query_len, max_query_len, query_offset, num_rows;
   const float* weights;
@@ -64,6 +68,13 @@ struct IndexerParams {
   int logits_width;
   int* err;
 };
+
+// Visible compressed blocks of row r: the caller's count, or derived.
+__device__ __forceinline__ int row_visible(const IndexerParams& p, int r) {
+  return p.visible != nullptr ? p.visible[r]
+                              : visible_of(p.positions, p.seq_lens, p.num_sequences,
+                                           p.token_to_req, p.ratio, r);
+}
 cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream);
 // tcgen05 + TMA formulation (indexer_tc.cu); launch_indexer dispatches to it
 // when indexer_tc_eligible() holds, else runs the mma.sync kernel.

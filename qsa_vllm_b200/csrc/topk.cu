@@ -235,7 +235,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   int32_t* out_row = p.output + static_cast<int64_t>(row) * p.out_row_stride;
   RowMeta m{};
   if (p.expand) m = row_meta(p, row);
-  const int length = min(max(p.lengths[row], 0), p.width);
+  const int length =
+      min(max(p.lengths != nullptr ? p.lengths[row]
+                                   : visible_of(p.positions, p.seq_lens, p.num_requests,
+                                                p.token_to_req, p.ratio, row),
+              0),
+          p.width);
 
   if (length <= topk) {
     // Every column is selected (topk.cu:187-191); no score is read.

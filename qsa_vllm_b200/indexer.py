@@ -23,6 +23,7 @@ import torch
 from . import _lib
 from .graph_dispatch import decode_logits_columns
 from .topk import topk_expand as _topk_expand
+from .topk import topk_expand_visible as _topk_expand_visible
 
 _INDEXER_WORKSPACE_BYTES = int(os.environ.get("QSA_INDEXER_WORKSPACE_MB", "64")) * 1024 * 1024
 
@@ -35,14 +36,19 @@ def indexer_scores(q: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Ten
                    visible: torch.Tensor, logits: torch.Tensor, *,
                    decode_query_len: int = 1, query_start_loc: torch.Tensor | None = None,
                    max_query_len: int = 0, query_offset: int = 0, num_rows: int | None = None,
-                   weights: torch.Tensor | None = None, scale: float | None = None) -> None:
+                   weights: torch.Tensor | None = None, scale: float | None = None,
+                   query_positions: torch.Tensor | None = None,
+                   sequence_lengths: torch.Tensor | None = None,
+                   token_to_req: torch.Tensor | None = None, compress_ratio: int = 0) -> None:
     """Write ``logits[r - query_offset, c]`` for the packed rows of this call.
 
     Decode (``query_start_loc is None``): ``q`` holds ``requests * decode_query_len``
     rows and ``page_table`` one row per request.  Prefill: ``q``/``visible`` are
     the full packed tensors indexed by absolute row, the call covers rows
     ``[query_offset, query_offset + num_rows)`` (as ``_prefill_logits``,
-    ops/indexer.py:282-302).
+    ops/indexer.py:282-302).  With ``visible=None`` the kernel derives each
+    row's count from ``query_positions`` / ``sequence_lengths`` /
+    ``token_to_req`` (indexed like ``visible``) and ``compress_ratio``.
     """
     rows = q.shape[0] if num_rows is None else num_rows
     if rows == 0:
@@ -52,8 +58,16 @@ def indexer_scores(q: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Ten
         raise TypeError("indexer q and key cache must be bfloat16")
     if logits.dtype != torch.float32 or logits.stride(-1) != 1:
         raise TypeError("logits must be float32 with unit column stride")
-    if page_table.dtype != torch.int32 or visible.dtype != torch.int32:
+    if page_table.dtype != torch.int32 or (visible is not None and visible.dtype != torch.int32):
         raise TypeError("page_table and visible must be int32")
+    if visible is None:
+        if query_positions is None or sequence_lengths is None or token_to_req is None \
+                or compress_ratio <= 0:
+            raise ValueError("visible=None needs query_positions, sequence_lengths, "
+                             "token_to_req and compress_ratio")
+        if query_positions.dtype != torch.int64 or sequence_lengths.dtype != torch.int32 \
+                or token_to_req.dtype != torch.int32:
+            raise TypeError("positions int64, sequence_lengths / token_to_req int32 expected")
     if q.stride(-1) != 1 or k_cache.stride(-1) != 1:
         raise ValueError("q and k_cache need a unit head-dim stride")
     w_ptr, w_rs, w_hs = None, 0, 0
@@ -75,7 +89,13 @@ def indexer_scores(q: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Ten
             k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.shape[0],
             k_cache.shape[1], page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
             page_table.shape[0] if qsl is None else qsl.numel() - 1,
-            visible.data_ptr(), None if qsl is None else qsl.data_ptr(),
+            None if visible is None else visible.data_ptr(),
+            None if visible is not None else query_positions.data_ptr(),
+            None if visible is not None else sequence_lengths.data_ptr(),
+            0 if visible is not None else sequence_lengths.numel(),
+            None if visible is not None else token_to_req.data_ptr(),
+            0 if visible is not None else int(compress_ratio),
+            None if qsl is None else qsl.data_ptr(),
             int(decode_query_len), int(max_query_len), int(query_offset), int(rows),
             w_ptr, w_rs, w_hs, float(scale), logits.data_ptr(), logits.stride(0),
             logits.shape[1], _lib.stream_ptr(q.device)), "indexer_scores")
@@ -118,24 +138,35 @@ def qsa_select_paged_decode(q, k_cache, page_table, visible_blocks, token_topk, 
         last = min(first + requests_per_chunk, num_requests)
         r0, r1 = first * decode_query_len, last * decode_query_len
         logits = logits_workspace[:r1 - r0]
-        indexer_scores(q[r0:r1], k_cache, page_table[first:last], visible_blocks[r0:r1], logits,
+        vis = None if visible_blocks is None else visible_blocks[r0:r1]
+        indexer_scores(q[r0:r1], k_cache, page_table[first:last], vis, logits,
                        decode_query_len=decode_query_len,
-                       weights=None if weights is None else weights[r0:r1], scale=scale)
-        _topk_expand(
-            logits, visible_blocks[r0:r1], query_positions[r0:r1], sequence_lengths,
-            token_to_req[r0:r1], out[r0:r1], compress_ratio,
-            main_block_table=main_block_table, main_page_size=main_page_size,
-            valid_counts_out=(valid_counts_out[r0:r1] if valid_counts_out is not None else None))
+                       weights=None if weights is None else weights[r0:r1], scale=scale,
+                       query_positions=query_positions[r0:r1],
+                       sequence_lengths=sequence_lengths, token_to_req=token_to_req[r0:r1],
+                       compress_ratio=compress_ratio)
+        select = dict(main_block_table=main_block_table, main_page_size=main_page_size,
+                      valid_counts_out=(valid_counts_out[r0:r1]
+                                        if valid_counts_out is not None else None))
+        if vis is None:
+            _topk_expand_visible(logits, query_positions[r0:r1], sequence_lengths,
+                                 token_to_req[r0:r1], out[r0:r1], compress_ratio, **select)
+        else:
+            _topk_expand(logits, vis, query_positions[r0:r1], sequence_lengths,
+                         token_to_req[r0:r1], out[r0:r1], compress_ratio, **select)
 
 
 def _prefill_logits(q, k_cache, page_table, query_start_loc, visible_blocks, logits_workspace,
                     max_query_len, logits_width, query_offset, num_queries, *, weights=None,
-                    scale=None):
+                    scale=None, query_positions=None, sequence_lengths=None, token_to_req=None,
+                    compress_ratio=0):
     """Score packed prefill rows [query_offset, query_offset+num_queries) (ops/indexer.py:282-302)."""
     logits = logits_workspace[:num_queries * logits_width].view(num_queries, logits_width)
     indexer_scores(q, k_cache, page_table, visible_blocks, logits,
                    query_start_loc=query_start_loc, max_query_len=max_query_len,
-                   query_offset=query_offset, num_rows=num_queries, weights=weights, scale=scale)
+                   query_offset=query_offset, num_rows=num_queries, weights=weights, scale=scale,
+                   query_positions=query_positions, sequence_lengths=sequence_lengths,
+                   token_to_req=token_to_req, compress_ratio=compress_ratio)
     return logits
 
 
@@ -156,13 +187,20 @@ def qsa_select_paged_prefill(q, k_cache, page_table, query_start_loc, visible_bl
         logits = _prefill_logits(q, k_cache, page_table, query_start_loc, visible_blocks,
                                  logits_workspace, max_query_len, logits_width,
                                  query_offset=start, num_queries=end - start,
-                                 weights=weights, scale=scale)
-        _topk_expand(
-            logits, visible_blocks[start:end], query_positions[start:end], sequence_lengths,
-            token_to_req[start:end], out[start:end], compress_ratio,
-            main_block_table=main_block_table, main_page_size=main_page_size,
-            valid_counts_out=(valid_counts_out[start:end] if valid_counts_out is not None
-                              else None))
+                                 weights=weights, scale=scale, query_positions=query_positions,
+                                 sequence_lengths=sequence_lengths, token_to_req=token_to_req,
+                                 compress_ratio=compress_ratio)
+        select = dict(main_block_table=main_block_table, main_page_size=main_page_size,
+                      valid_counts_out=(valid_counts_out[start:end]
+                                        if valid_counts_out is not None else None))
+        if visible_blocks is None:
+            _topk_expand_visible(logits, query_positions[start:end], sequence_lengths,
+                                 token_to_req[start:end], out[start:end], compress_ratio,
+                                 **select)
+        else:
+            _topk_expand(logits, visible_blocks[start:end], query_positions[start:end],
+                         sequence_lengths, token_to_req[start:end], out[start:end],
+                         compress_ratio, **select)
 
 
 def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, sequence_lengths,
@@ -182,12 +220,16 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
     if not rows:
         return out
     if visible_blocks is None:
+        # One small launch: the counts it writes stay in L2 for both the
+        # indexer and the top-k.  (Both kernels can also derive them per row,
+        # visible_blocks=None below, but each then pays a dependent
+        # token_to_req -> sequence_lengths load before its first real work.)
         visible_blocks = compute_visible_blocks(query_positions, sequence_lengths, token_to_req,
                                                 compress_ratio)
     if num_decode_tokens:
         qsa_select_paged_decode(
             q[:num_decode_tokens], k_cache, page_table[:num_decodes],
-            visible_blocks[:num_decode_tokens], token_topk, compress_ratio, decode_query_len,
+            None if visible_blocks is None else visible_blocks[:num_decode_tokens], token_topk, compress_ratio, decode_query_len,
             out[:num_decode_tokens], max_seq_len,
             query_positions=query_positions[:num_decode_tokens],
             sequence_lengths=sequence_lengths, token_to_req=token_to_req[:num_decode_tokens],
@@ -198,7 +240,8 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
     if num_decode_tokens < rows:
         qsa_select_paged_prefill(
             q[num_decode_tokens:], k_cache, page_table[num_decodes:],
-            query_start_loc[num_decodes:], visible_blocks[num_decode_tokens:], token_topk,
+            query_start_loc[num_decodes:],
+            None if visible_blocks is None else visible_blocks[num_decode_tokens:], token_topk,
             compress_ratio, max_query_len, out[num_decode_tokens:], max_seq_len,
             query_positions=query_positions[num_decode_tokens:],
             sequence_lengths=sequence_lengths, token_to_req=token_to_req[num_decode_tokens:],

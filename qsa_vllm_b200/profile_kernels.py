@@ -20,7 +20,7 @@ import json
 
 import torch
 
-from .indexer import indexer_scores, select_paged_tokens
+from .indexer import compute_visible_blocks, indexer_scores, select_paged_tokens
 from .qsa import qsa_sparse_paged_attention
 from .synthetic import make_workload
 from .topk import topk_expand
@@ -36,6 +36,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--contiguous-tables", action="store_true")
     ap.add_argument("--time", action="store_true")
+    ap.add_argument("--visible-kernel", action="store_true",
+                    help="step: compute visible counts with qsa_visible_blocks first and "
+                         "pass them in (instead of the kernels deriving them)")
     a = ap.parse_args()
     dev = torch.device("cuda")
     w = make_workload(a.config, device=dev, seed=0, batch=a.batch)
@@ -76,12 +79,14 @@ def main() -> None:
                                    indices_are_physical=True, valid_counts=cnt)
 
     def run_step():
+        given = (compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, r)
+                 if a.visible_kernel else None)
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
             w.token_topk, r, idx, query_start_loc=w.query_start_loc, max_query_len=1,
             max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt,
-            weights=w.index_weights, scale=w.index_scale)
+            weights=w.index_weights, scale=w.index_scale, visible_blocks=given)
         run_attention()
 
     run_indexer()

@@ -32,9 +32,20 @@ def _topk_expand_impl(scores, lengths, positions, sequence_lengths, token_to_req
     rows = scores.shape[0]
     if rows == 0:
         return
+    _require(lengths, torch.int32, "lengths")
+    _topk_expand_call(scores, lengths, positions, sequence_lengths, token_to_req, table,
+                      output, counts, ratio, page_size, physical, store_counts)
+
+
+def _topk_expand_call(scores, lengths, positions, sequence_lengths, token_to_req, table,
+                      output, counts, ratio, page_size, physical, store_counts) -> None:
+    """qsa_topk_expand; ``lengths=None`` lets the kernel derive each row's
+    visible block count from positions / sequence_lengths / token_to_req."""
+    rows = scores.shape[0]
+    if rows == 0:
+        return
     _lib.ensure_device(scores.device)
     _require(scores, torch.float32, "scores")
-    _require(lengths, torch.int32, "lengths")
     _require(positions, torch.int64, "positions")
     _require(sequence_lengths, torch.int32, "sequence_lengths")
     _require(token_to_req, torch.int32, "token_to_req")
@@ -49,7 +60,8 @@ def _topk_expand_impl(scores, lengths, positions, sequence_lengths, token_to_req
     with torch.cuda.device(scores.device):
         _lib.check(lib.qsa_topk_expand(
             scores.data_ptr(), scores.stride(0), rows, scores.shape[1],
-            lengths.data_ptr(), positions.data_ptr(), sequence_lengths.data_ptr(),
+            None if lengths is None else lengths.data_ptr(), positions.data_ptr(),
+            sequence_lengths.data_ptr(),
             sequence_lengths.numel(), token_to_req.data_ptr(),
             table.data_ptr() if physical else None,
             table.stride(0) if physical else 0, table.shape[1] if physical else 0,
@@ -117,4 +129,18 @@ def topk_expand(scores, lengths, query_positions, sequence_lengths, token_to_req
     )
 
 
-__all__ = ["topk", "topk_expand"]
+def topk_expand_visible(scores, query_positions, sequence_lengths, token_to_req, output,
+                        compress_ratio, *, main_block_table=None, main_page_size=1,
+                        valid_counts_out=None):
+    """``topk_expand`` with each row's length computed in the kernel as its
+    visible block count min((pos + 1) // r, seq_len // r) (ops/indexer.py:363-369),
+    so no visible-count tensor is built first."""
+    _topk_expand_call(
+        scores, None, query_positions, sequence_lengths, token_to_req,
+        main_block_table if main_block_table is not None else output,
+        output, valid_counts_out if valid_counts_out is not None else output,
+        compress_ratio, main_page_size, main_block_table is not None,
+        valid_counts_out is not None)
+
+
+__all__ = ["topk", "topk_expand", "topk_expand_visible"]

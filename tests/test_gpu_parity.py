@@ -270,6 +270,41 @@ def test_indexer_rejects_decode_rows_without_table_rows(dev):
         indexer_scores(q.to(dev), kc.to(dev), table[:2].to(dev), vis.to(dev), logits)
 
 
+@pytest.mark.parametrize("config", ["cfg2", "cfg0"])
+def test_kernels_derive_visible_counts_like_the_visible_kernel(dev, config):
+    """visible_blocks=None: the indexer and top-k kernels derive each row's
+    count themselves; results equal the path fed by qsa_visible_blocks."""
+    from qsa_vllm_b200.indexer import compute_visible_blocks, indexer_scores
+    from qsa_vllm_b200.synthetic import make_workload
+    from qsa_vllm_b200.topk import topk_expand, topk_expand_visible
+    w = make_workload(config, device=dev, seed=3, batch=16)
+    vis = compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, w.ratio)
+    cols = w.index_table.shape[1] * w.index_cache.shape[1]
+    a = torch.full((w.rows, cols), float("nan"), device=dev)
+    b = torch.full((w.rows, cols), float("nan"), device=dev)
+    common = dict(weights=w.index_weights, scale=w.index_scale)
+    indexer_scores(w.index_q, w.index_cache, w.index_table, vis, a, **common)
+    indexer_scores(w.index_q, w.index_cache, w.index_table, None, b, query_positions=w.positions,
+                   sequence_lengths=w.seq_lens, token_to_req=w.token_to_req,
+                   compress_ratio=w.ratio, **common)
+    assert torch.equal(torch.isnan(a), torch.isnan(b)) and torch.equal(a.nan_to_num(), b.nan_to_num())
+    width = w.token_topk + w.ratio - 1
+    outs = []
+    for derived in (False, True):
+        out = torch.empty(w.rows, width, dtype=torch.int32, device=dev)
+        cnt = torch.empty(w.rows, dtype=torch.int32, device=dev)
+        kw = dict(main_block_table=w.block_table, main_page_size=w.page_size,
+                  valid_counts_out=cnt)
+        if derived:
+            topk_expand_visible(a.nan_to_num(), w.positions, w.seq_lens, w.token_to_req, out,
+                                w.ratio, **kw)
+        else:
+            topk_expand(a.nan_to_num(), vis, w.positions, w.seq_lens, w.token_to_req, out,
+                        w.ratio, **kw)
+        outs.append((out, cnt))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
 # ---------------------------------------------------------------- attention
 def _attention_check(got: torch.Tensor, ref: torch.Tensor):
     got = got.float().cpu()

@@ -59,8 +59,14 @@ def test_argument_errors_are_reported_not_launched():
                              7, None, 0, 16, 1, None)
     assert st == 1 and b"ratio" in lib.qsa_last_error()
     st = lib.qsa_indexer_scores(1024, 64, 64, 4, 96, 1024, 0, 0, 1, 16, 1024, 0, 1, 1, 1024,
+                                None, None, 0, None, 0,
                                 None, 1, 1, 0, 1, None, 0, 0, 1.0, 1024, 0, 8, None)
     assert st == 2 and b"head_dim" in lib.qsa_last_error()
+    # no visible counts and nothing to derive them from
+    st = lib.qsa_indexer_scores(1024, 64, 64, 4, 64, 1024, 0, 0, 1, 16, 1024, 0, 1, 1, None,
+                                None, None, 0, None, 0,
+                                None, 1, 1, 0, 1, None, 0, 0, 1.0, 1024, 0, 8, None)
+    assert st == 1 and b"positions" in lib.qsa_last_error()
     st = lib.qsa_sparse_attention(1024, 0, 0, 1, 48, 128, 1024, 0, 0, 0, 1024, 0, 0, 0, 1, 16,
                                   2, 1024, 0, 8, None, 0, 0, 0, None, None, None, 0, 0, 0, 1024,
                                   0, 0, 1, 1, None, 0, None)
@@ -207,16 +213,21 @@ def test_head_sharded_attention_two_gloo_ranks(tmp_path):
 
 
 # -------------------------------------------------- indexer host chunking
-def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch):
-    """The host loop (workspace chunks, decode/prefill split, visible blocks)
-    driven with the oracle standing in for the two kernels must reproduce the
-    oracle's one-shot result."""
+@pytest.mark.parametrize("given_visible", [False, True])
+def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch, given_visible):
+    """The host loop (workspace chunks, decode/prefill split, visible blocks
+    given or derived in the kernels) driven with the oracle standing in for the
+    two kernels must reproduce the oracle's one-shot result."""
     import qsa_vllm_b200.indexer as I
 
     def fake_scores(q, k_cache, page_table, visible, logits, *, decode_query_len=1,
                     query_start_loc=None, max_query_len=0, query_offset=0, num_rows=None,
-                    weights=None, scale=None):
+                    weights=None, scale=None, query_positions=None, sequence_lengths=None,
+                    token_to_req=None, compress_ratio=0):
         rows = q.shape[0] if num_rows is None else num_rows
+        if visible is None:   # what the kernel derives (same row indexing as q)
+            visible = O.visible_blocks(query_positions, sequence_lengths, token_to_req,
+                                       compress_ratio)
         if query_start_loc is None:
             res = O.indexer_scores(q, k_cache, page_table, visible, logits.shape[1],
                                    decode_query_len=decode_query_len, weights=weights,
@@ -235,10 +246,13 @@ def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch):
         if valid_counts_out is not None:
             valid_counts_out.copy_(torch.from_numpy(counts))
 
+    def fake_topk_visible(scores, positions, seq_lens, t2r, output, ratio, **kw):
+        fake_topk(scores, O.visible_blocks(positions, seq_lens, t2r, ratio), positions,
+                  seq_lens, t2r, output, ratio, **kw)
+
     monkeypatch.setattr(I, "indexer_scores", fake_scores)
     monkeypatch.setattr(I, "_topk_expand", fake_topk)
-    monkeypatch.setattr(I, "compute_visible_blocks",
-                        lambda pos, seq, t2r, ratio: O.visible_blocks(pos, seq, t2r, ratio))
+    monkeypatch.setattr(I, "_topk_expand_visible", fake_topk_visible)
     monkeypatch.setattr(I, "_INDEXER_WORKSPACE_BYTES", 3 * 64 * 4)   # force many chunks
     g = torch.Generator().manual_seed(0)
     ratio, page, topk = 4, 16, 32
@@ -252,9 +266,10 @@ def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch):
     table = torch.randperm(nblk, generator=g)[:15].view(3, 5).to(torch.int32)
     q = torch.randn(7, 4, 64, generator=g).to(torch.bfloat16)
     out = torch.empty(7, topk + ratio - 1, dtype=torch.int32)
-    I.select_paged_tokens(q, kc, table, t2r, pos, seq, topk, ratio, out, query_start_loc=qsl,
-                          max_query_len=5, max_seq_len=300, num_decodes=2, num_decode_tokens=2)
     vis = O.visible_blocks(pos, seq, t2r, ratio)
+    I.select_paged_tokens(q, kc, table, t2r, pos, seq, topk, ratio, out, query_start_loc=qsl,
+                          max_query_len=5, max_seq_len=300, num_decodes=2, num_decode_tokens=2,
+                          visible_blocks=vis.clone() if given_visible else None)
     logits = torch.zeros(7, 80)
     for r in range(7):
         req = int(t2r[r])
