@@ -253,6 +253,8 @@ def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch, given_vis
     monkeypatch.setattr(I, "indexer_scores", fake_scores)
     monkeypatch.setattr(I, "_topk_expand", fake_topk)
     monkeypatch.setattr(I, "_topk_expand_visible", fake_topk_visible)
+    monkeypatch.setattr(I, "compute_visible_blocks",
+                        lambda pos, seq, t2r, ratio: O.visible_blocks(pos, seq, t2r, ratio))
     monkeypatch.setattr(I, "_INDEXER_WORKSPACE_BYTES", 3 * 64 * 4)   # force many chunks
     g = torch.Generator().manual_seed(0)
     ratio, page, topk = 4, 16, 32
