@@ -65,11 +65,12 @@ struct TcCfg {
   static constexpr int kSubBytes = kTileKeys * 128;    // one MMA tile, one sub-row: 16 KB
   static constexpr int kStageBytes = MT * kSub * kSubBytes;  // 32 KB
   static constexpr int kQSubBytes = NQ * 128;
-  // stages in flight: as many 32 KB stages as fit beside the two query slots
-  // (more bytes in flight per SM hide more DRAM latency)
-  static constexpr int kSmemBudget = 220 * 1024;
+  // stages in flight: the 32 KB stages that fit beside the two query slots in
+  // half of an SM's shared memory, so two CTAs share an SM (two independent
+  // pipelines per SM, half-size work ranges); at least two stages
+  static constexpr int kSmemBudget = 110 * 1024;
   static constexpr int kFit = (kSmemBudget - 2 * kSub * kQSubBytes) / (MT * kSub * kTileKeys * 128);
-  static constexpr int S = kFit > 8 ? 8 : kFit;
+  static constexpr int S = kFit > 8 ? 8 : (kFit < 2 ? 2 : kFit);
   static constexpr int kAccCols = MT * NQ;             // TMEM columns of one stage's scores
   static constexpr int A = kAccCols <= 64 ? 4 : 2;     // accumulator ring (even: one group each)
   static constexpr int kCols = A * kAccCols < 32 ? 32 : A * kAccCols;
