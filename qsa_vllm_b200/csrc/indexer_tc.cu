@@ -244,42 +244,58 @@ __device__ __forceinline__ void score_columns_pow2_reg(const uint32_t* v, const 
       out[static_cast<int64_t>(x >> hshift) * row_stride + key] = r[x] * scale;
 }
 
-// Epilogue arithmetic for a power-of-two head count (H = 1 << hshift): the
-// heads of a row are summed by a log-depth tree over the chunk's columns
-// (every predicate is warp-uniform), then row sums are stored.  A row wider
-// than the chunk (H > N) is carried in `carry` and stored by its last chunk.
-template <int N>
-__device__ __forceinline__ void score_columns_pow2(const uint32_t* v, const float* wv, int c0,
-                                                   int H, int hshift, float& carry,
-                                                   int rows_here, const int* lim, float* out,
-                                                   int64_t row_stride, int key, float scale) {
+// Epilogue arithmetic for a power-of-two head count H, fixed at compile time:
+// the heads of a row are summed by a log-depth tree over the chunk's columns,
+// then the chunk's N/H row sums are stored (one limit load and one store per
+// row).  A row wider than the chunk (H > N) is carried in `carry` and stored
+// by its last chunk.
+template <int N, int H>
+__device__ __forceinline__ void score_columns_h(const uint32_t* v, const float* wv, int c0,
+                                                float& carry, int rows_here, const int* lim,
+                                                float* out, int64_t row_stride, int key,
+                                                float scale) {
   float r[N];
 #pragma unroll
   for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+  constexpr int kSpan = H < N ? H : N;  // columns summed per tree
 #pragma unroll
-  for (int step = 1; step < N; step <<= 1) {
-    if (step < H) {
+  for (int step = 1; step < kSpan; step <<= 1) {
 #pragma unroll
-      for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
-    }
+    for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
   }
-  if (H <= N) {
+  if constexpr (H <= N) {
 #pragma unroll
-    for (int x = 0; x < N; ++x) {
-      if ((x & (H - 1)) == 0) {
-        const int ri = (c0 + x) >> hshift;
-        if (ri < rows_here && key < lim[ri])
-          out[static_cast<int64_t>(ri) * row_stride + key] = r[x] * scale;
-      }
+    for (int j = 0; j < N / H; ++j) {
+      const int ri = c0 / H + j;
+      if (ri < rows_here && key < lim[ri])
+        out[static_cast<int64_t>(ri) * row_stride + key] = r[j * H] * scale;
     }
   } else {
     carry += r[0];
-    if (((c0 + N) & (H - 1)) == 0) {
-      const int ri = c0 >> hshift;
+    if ((c0 + N) % H == 0) {
+      const int ri = c0 / H;
       if (ri < rows_here && key < lim[ri])
         out[static_cast<int64_t>(ri) * row_stride + key] = carry * scale;
       carry = 0.f;
     }
+  }
+}
+
+// Power-of-two head count H = 1 << hshift (warp-uniform dispatch).
+template <int N>
+__device__ __forceinline__ void score_columns_pow2(const uint32_t* v, const float* wv, int c0,
+                                                   int hshift, float& carry, int rows_here,
+                                                   const int* lim, float* out,
+                                                   int64_t row_stride, int key, float scale) {
+  switch (hshift) {
+    case 0: score_columns_h<N, 1>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 1: score_columns_h<N, 2>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 2: score_columns_h<N, 4>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 3: score_columns_h<N, 8>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 4: score_columns_h<N, 16>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 5: score_columns_h<N, 32>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    case 6: score_columns_h<N, 64>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+    default: score_columns_h<N, 128>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
   }
 }
 
@@ -579,7 +595,7 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
                                          p.logits_row_stride, key, scale);
             } else if (hshift >= 0) {
               float carry = 0.f;
-              score_columns_pow2<CH>(v + mt * NQ, wv, 0, H, hshift, carry, rows_here, lim, out,
+              score_columns_pow2<CH>(v + mt * NQ, wv, 0, hshift, carry, rows_here, lim, out,
                                      p.logits_row_stride, key, scale);
             } else {
               float acc = 0.f;
@@ -589,20 +605,22 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
             }
           }
         } else {
-          // 64 columns per round of loads; a row may span rounds
-#pragma unroll
+          // 64 columns per round of loads; a row may span rounds.  The
+          // rounds share one copy of the (unrolled) 64-column body: unrolled
+          // rounds would outgrow the instruction cache.
+#pragma unroll 1
           for (int mt = 0; mt < MT; ++mt) {
             const int key = key0 + mt * kTileKeys;
             float acc = 0.f;
             int h = 0, ri = 0;
-#pragma unroll
+#pragma unroll 1
             for (int c0 = 0; c0 < NQ; c0 += CH) {
               uint32_t v[CH];
 #pragma unroll
               for (int c = 0; c < CH; c += 16) tmem_ld16(acc_base + mt * NQ + c0 + c, v + c);
               tmem_wait_ld();
               if (hshift >= 0)
-                score_columns_pow2<CH>(v, wv, c0, H, hshift, acc, rows_here, lim, out,
+                score_columns_pow2<CH>(v, wv, c0, hshift, acc, rows_here, lim, out,
                                        p.logits_row_stride, key, scale);
               else
                 score_columns_seq<CH>(v, wv, c0, H, acc, h, ri, rows_here, lim, out,
@@ -671,10 +689,25 @@ cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& kmap, const CUt
   cudaError_t e = set_attr_once(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTcThreads, smem);
+  // all of the SM's unified L1/shared storage as shared memory, so that two
+  // CTAs' stage rings fit on one SM
+  e = set_attr_once(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                    cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  per_sm = std::max(1, std::min(per_sm, 512 / C::kCols));  // resident CTAs share 512 columns
+  // Resident CTAs per SM from the SM's shared memory and registers (each CTA
+  // also reserves 1 KB of shared memory), capped by the 512 TMEM columns.
+  int dev = 0, sm_smem = 0, sm_regs = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&sm_regs, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+  cudaFuncAttributes fa{};
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fn);
+  if (e != cudaSuccess) return e;
+  const int by_smem = sm_smem / static_cast<int>(smem + 1024);
+  const int by_regs = sm_regs / std::max(1, fa.numRegs * kTcThreads);
+  const int per_sm = std::max(1, std::min({by_smem, by_regs, 512 / C::kCols}));
   const int64_t ctas = std::min<int64_t>(g.units, static_cast<int64_t>(num_sms()) * per_sm);
   return count_launches(launch_kernel(indexer_tc_kernel<D, NQ>, dim3(static_cast<int>(ctas)),
                                       dim3(kTcThreads), smem, stream, 1, kmap, qmap, p, g));

@@ -81,10 +81,12 @@ def main() -> None:
     def run_step():
         given = (compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, r)
                  if a.visible_kernel else None)
+        decodes = rows if w.is_decode else 0   # prefill configs: packed prefill rows only
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
-            w.token_topk, r, idx, query_start_loc=w.query_start_loc, max_query_len=1,
-            max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            w.token_topk, r, idx, query_start_loc=w.query_start_loc,
+            max_query_len=1 if w.is_decode else w.max_query_len,
+            max_seq_len=w.max_seq_len, num_decodes=decodes, num_decode_tokens=decodes,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt,
             weights=w.index_weights, scale=w.index_scale, visible_blocks=given)
         run_attention()
