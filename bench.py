@@ -8,7 +8,9 @@ indexer 8 heads x 64 with U(0,1) head weights, compress ratio 4, top-k 2048
 tokens (512 blocks), page 64, seeded random block tables.  A step is the whole
 QSA path of one layer for those 64 rows, run as vLLM runs decode: through the
 drop-in operators (``select_paged_tokens`` + ``qsa_sparse_paged_attention``)
-captured in a CUDA graph.  Inputs are synthetic (seeded N(0,1) / U(0,1)).
+captured in a CUDA graph, with the per-step metadata the reference layer
+receives (block tables, positions, sequence lengths and visible block counts,
+reference attention.py:128-142).  Inputs are synthetic (seeded N(0,1) / U(0,1)).
 
 Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on
 the launching stream, with the L2 flushed before every step outside the
@@ -254,7 +256,7 @@ def main() -> None:
                                 device_id=dev)
 
     from qsa_vllm_b200 import _lib
-    from qsa_vllm_b200.indexer import select_paged_tokens
+    from qsa_vllm_b200.indexer import compute_visible_blocks, select_paged_tokens
     from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
     from qsa_vllm_b200.synthetic import make_workload
 
@@ -273,11 +275,17 @@ def main() -> None:
         flush_w.zero_()   # evicts the previous step's lines (leaves dirty flush lines) ...
         flush_r.sum()     # ... which a clean read then writes back, outside the timed region
 
+    # Per-step metadata, as the reference layer receives it: visible_blocks
+    # comes with vLLM's compressed-cache metadata (reference attention.py:139),
+    # built once per step for every QSA layer, like the block tables.
+    w.visible_blocks = compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, w.ratio)
+
     def step():
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
             w.token_topk, w.ratio, idx_buf, query_start_loc=w.query_start_loc, max_query_len=1,
             max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            visible_blocks=w.visible_blocks,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt_buf,
             weights=w.index_weights, scale=w.index_scale)
         qsa_sparse_paged_attention(w.q, w.k_cache, w.v_cache, idx_buf, w.block_table,
@@ -370,7 +378,8 @@ def main() -> None:
             setattr(w, n, view)   # the step now reads its inputs from the staged buffer
         return d, h
     dev_meta, host_meta = stage(("index_q", "index_weights", "positions", "seq_lens",
-                                 "token_to_req", "block_table", "index_table"))
+                                 "token_to_req", "visible_blocks", "block_table",
+                                 "index_table"))
     dev_qg, host_qg = stage(("q", "gate"))
     host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     h2d = dev_meta.numel() + dev_qg.numel()
@@ -389,6 +398,7 @@ def main() -> None:
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
             w.token_topk, w.ratio, idx_buf, query_start_loc=w.query_start_loc, max_query_len=1,
             max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            visible_blocks=w.visible_blocks,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt_buf,
             weights=w.index_weights, scale=w.index_scale)
         main.wait_event(qg_ready)

@@ -79,8 +79,10 @@ def main() -> None:
                                    indices_are_physical=True, valid_counts=cnt)
 
     def run_step():
+        # visible counts arrive with the step's metadata (as in the reference
+        # layer), unless --visible-kernel recomputes them inside the step
         given = (compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, r)
-                 if a.visible_kernel else None)
+                 if a.visible_kernel else vis)
         decodes = rows if w.is_decode else 0   # prefill configs: packed prefill rows only
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
