@@ -7,8 +7,8 @@
 // length is <= K emit 0..length-1.
 //
 // Design (B200), latency first (a decode step selects over only ~2-8 MB):
-//   * one CTA of 512 threads per row slice; each thread keeps its keys (16,
-//     or 64 for very wide rows) in REGISTERS after one coalesced 16-byte load
+//   * one CTA of 1024 threads per row slice; each thread keeps its keys (8,
+//     or 32 for very wide rows) in REGISTERS after one coalesced 16-byte load
 //     pass from HBM, so every radix pass re-reads registers, not memory;
 //   * radix select, most-significant digit first, in digits of up to 11
 //     bits below the high bits shared by every key of the row (found from the
@@ -37,7 +37,7 @@ namespace cg = cooperative_groups;
 namespace qsa {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 2048;
 constexpr int kMaxCluster = 16;
@@ -481,23 +481,23 @@ cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
 
 }  // namespace
 
-int topk_max_width() { return kMaxCluster * kThreads * 64; }
+int topk_max_width() { return kMaxCluster * kThreads * 32; }
 
 cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_cluster) {
   TopkParams p = p0;
   if (p.rows <= 0) return cudaSuccess;
   // Smallest (keys per thread, cluster width) whose slices cover the row.
   const int w = std::max(p.width, 1);
-  int V = 16;
+  int V = 8;
   int C = pow2_ceil((w + kThreads * V - 1) / (kThreads * V));
   if (C > kMaxCluster) {
-    V = 64;
+    V = 32;
     C = pow2_ceil((w + kThreads * V - 1) / (kThreads * V));
   }
   if (C > kMaxCluster) return cudaErrorInvalidValue;
   p.slice_cap = kThreads * V;
   if (plan_cluster) *plan_cluster = C;
-  return V == 16 ? launch_v<16>(p, C, stream) : launch_v<64>(p, C, stream);
+  return V == 8 ? launch_v<8>(p, C, stream) : launch_v<32>(p, C, stream);
 }
 
 }  // namespace qsa
