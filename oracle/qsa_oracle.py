@@ -14,6 +14,9 @@ It restates in numpy / PyTorch-eager CPU code what the reference plugin
                            a second statement of the same expansion rules)
 5. ``sparse_attention``    ops/qsa.py:109-303 (split-K paged GQA kernel),
                            :306-362 (split merge), :594-688 (launch table)
+6. ``qsa_prepare``         ops/prepare.py:16-46 (norm + RoPE with bf16 rounding
+                           steps), :49-166 (index queries, key compression,
+                           raw-key ring commit, main K/V cache writes)
 
 Parity pin.  The reference ships no tests or golden vectors.  This oracle is
 pinned against fixtures produced from the reference itself:
@@ -454,7 +457,137 @@ def decode_step(w, *, round_p: bool = True):
     return out, idx, counts, logits
 
 
+def _bf16_trunc(x: torch.Tensor) -> torch.Tensor:
+    """fp32 -> bf16 rounding toward zero (low 16 bits cleared), returned as fp32."""
+    return (x.float().contiguous().view(torch.int32) & -65536).view(torch.float32)
+
+
+def norm_rope(x: torch.Tensor, positions: torch.Tensor, gamma: torch.Tensor,
+              cos_sin: torch.Tensor, eps: float, rotary: int, *,
+              rounding: str = "nearest") -> torch.Tensor:
+    """RMSNorm + rotate-half RoPE over the first ``rotary`` dims with the
+    reference's bf16 rounding after every post-norm step (ops/prepare.py:16-46).
+
+    x: [n, dim] (bf16 values); positions: [n]; gamma: [dim]; cos_sin:
+    [max_pos, rotary] with cosines in the first half, sines in the second.
+    Returns fp32 holding bf16 values.  ``rounding``: "nearest" (the GPU's
+    round-to-nearest-even conversion) or "truncate" (the Triton CPU
+    interpreter's conversion, for checking against interpreter fixtures).
+    """
+    _bf16r = _bf16 if rounding == "nearest" else _bf16_trunc
+    x = x.float()
+    dim = x.shape[1]
+    inv_rms = torch.rsqrt((x * x).sum(dim=1) / dim + eps)
+    normalized = _bf16r(x * inv_rms[:, None])
+    scaled = _bf16r(normalized * gamma.float()[None, :])
+    half = rotary // 2
+    dims = torch.arange(dim)
+    partner_dims = torch.where(dims < half, dims + half, dims - half).clamp(max=dim - 1)
+    partner = scaled[:, partner_dims]
+    rotated = _bf16r(torch.where(dims[None, :] < half, -partner, partner))
+    channel = dims % max(half, 1)
+    in_rot = dims < rotary
+    pos = positions.long()
+    cs = cos_sin.float()
+    cosine = torch.where(in_rot[None, :], cs[pos][:, channel.clamp(max=rotary - 1)],
+                         torch.zeros(()))
+    sine = torch.where(in_rot[None, :], cs[pos][:, (half + channel).clamp(max=rotary - 1)],
+                       torch.zeros(()))
+    first = _bf16r(scaled * cosine)
+    second = _bf16r(rotated * sine)
+    combined = _bf16r(first + second)
+    return torch.where(in_rot[None, :], combined, scaled)
+
+
+def qsa_prepare(index_qk: torch.Tensor, positions: torch.Tensor, q_weight: torch.Tensor,
+                k_weight: torch.Tensor, cos_sin: torch.Tensor, eps: float,
+                state_cache: torch.Tensor, state_slots: torch.Tensor,
+                state_table: torch.Tensor, query_start_loc: torch.Tensor,
+                logical_positions: torch.Tensor, compressed_cache: torch.Tensor,
+                compressed_slots: torch.Tensor, k_work: torch.Tensor,
+                main_key: torch.Tensor, main_value: torch.Tensor,
+                main_key_cache: torch.Tensor, main_value_cache: torch.Tensor,
+                main_slots: torch.Tensor, *, num_index_heads: int, index_head_dim: int,
+                rotary_dim: int, compress_ratio: int,
+                rounding: str = "nearest") -> torch.Tensor:
+    """The reference's one-launch indexer preparation (ops/prepare.py:49-228),
+    updating the four caches in place and returning the index queries.
+
+    * index queries (:99-118): RMSNorm + RoPE of each head's row of
+      ``index_qk`` at the token's position, with ``q_weight``;
+    * key compression (:120-152): per (request, work item) of ``k_work``, the
+      mean of ``compress_ratio`` raw keys ending at the group boundary (from this
+      chunk's ``index_qk`` key part, or from the request's ring ``state_cache``
+      for positions before the chunk), rounded to bf16, then RMSNorm + RoPE at
+      the group's first position with ``k_weight``, stored at the boundary
+      token's compressed slot;
+    * ring commit (:154-166): work item 0 of a request writes the chunk's last
+      ``min(query_len, state_size)`` raw keys to their state slots, after its
+      own group has read the ring;
+    * main K/V (:81-97): each token's key / value rows to ``main_slots``.
+    Slots < 0 are skipped.  Tensors hold bf16 values (fp32 or bf16 storage).
+    ``rounding`` as in ``norm_rope``.
+    """
+    H, D, R = num_index_heads, index_head_dim, compress_ratio
+    tokens = index_qk.shape[0]
+    qk = index_qk.float()
+    state_size = state_cache.shape[1]
+    comp_page = compressed_cache.shape[1]
+    # index queries
+    rows = qk[:, :H * D].reshape(tokens * H, D)
+    pos_rows = positions.long().repeat_interleave(H)
+    query = norm_rope(rows, pos_rows, q_weight, cos_sin, eps, rotary_dim,
+                      rounding=rounding).reshape(tokens, H, D)
+    _bf16r = _bf16 if rounding == "nearest" else _bf16_trunc
+    # key compression + ring commit, work item by work item (item 0 first
+    # within a request: its group reads the ring before the commit)
+    key_part = qk[:, H * D:H * D + D]
+    for request, work in k_work.tolist():
+        if request < 0:
+            continue
+        q0, q1 = int(query_start_loc[request]), int(query_start_loc[request + 1])
+        qlen = q1 - q0
+        chunk_end = int(logical_positions[q1 - 1])
+        chunk_start = chunk_end - qlen + 1
+        groups = (chunk_end + 1) // R - chunk_start // R
+        if work < groups:
+            first_boundary = ((chunk_start + R) // R) * R - 1
+            end = first_boundary + work * R
+            boundary_token = q0 + end - chunk_start
+            block = int(state_table[request, 0])
+            acc = torch.zeros(D)
+            for m in range(R):
+                src = end - (R - 1) + m
+                if src >= chunk_start:
+                    acc = acc + key_part[q0 + src - chunk_start]
+                else:
+                    acc = acc + state_cache[block, src % state_size].float()
+            pooled = _bf16r(acc / R)
+            comp = norm_rope(pooled[None, :], torch.tensor([end - (R - 1)]), k_weight,
+                             cos_sin, eps, rotary_dim, rounding=rounding)[0]
+            cslot = int(compressed_slots[boundary_token])
+            if cslot >= 0:
+                compressed_cache[cslot // comp_page, cslot % comp_page] = \
+                    comp.to(compressed_cache.dtype)
+        if work == 0:
+            suffix = min(qlen, state_size)
+            for t in range(q1 - suffix, q1):
+                slot = int(state_slots[t])
+                if slot >= 0:
+                    state_cache[slot // state_size, slot % state_size] = \
+                        key_part[t].to(state_cache.dtype)
+    # main K/V
+    main_page = main_key_cache.shape[1]
+    for t in range(tokens):
+        slot = int(main_slots[t])
+        if slot >= 0:
+            main_key_cache[slot // main_page, slot % main_page] = main_key[t]
+            main_value_cache[slot // main_page, slot % main_page] = main_value[t]
+    return query
+
+
 __all__ = [
+    "norm_rope", "qsa_prepare",
     "visible_blocks", "indexer_scores", "select_blocks", "topk_expand", "topk_plain",
     "expand_block_indices", "reference_launch_config", "sparse_attention",
     "decode_step", "float_bits", "LOG2E",

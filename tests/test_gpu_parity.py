@@ -94,7 +94,7 @@ def test_topk_expand_strided_output(dev):
                                              (64, 8192, 512), (300, 2048, 256),
                                              (3, 70000, 4096), (1, 200000, 2048)])
 def test_topk_expand_cluster_widths(dev, rows, width, topk):
-    """Cluster widths 1..16 CTAs per row, 16 or 64 keys per thread (set by the width)."""
+    """Cluster widths 1..16 CTAs per row, 8 or 32 keys per thread (set by the width)."""
     for kind in ("relu", "ties"):
         case = make_case(rows * 7 + width, rows, width, topk * 4, kind=kind, lengths="full")
         got, counts = run_topk_expand(case, dev)

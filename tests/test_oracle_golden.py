@@ -140,3 +140,31 @@ def test_select_blocks_bit_order_semantics():
     assert list(O.select_blocks(row, 7, 5)) == [0, 1, 2, 3, 5]
     assert list(O.select_blocks(row, 2, 3)) == [0, 1, -1]
     assert list(O.select_blocks(row, 0, 2)) == [-1, -1]
+
+
+# ------------------------------------------------------------- qsa_prepare
+def _prepare_inputs(d, name):
+    g = lambda k: torch.from_numpy(d[f"{name}_in_{k}"].copy())  # noqa: E731
+    consts = {k: int(d[f"{name}_in_{k}"]) for k in ("heads", "dim", "rotary", "ratio")}
+    return g, consts, float(d[f"{name}_in_eps"])
+
+
+@pytest.mark.parametrize("name", ["rot64", "rot32"])
+def test_prepare_oracle_matches_reference_interpreter(name):
+    """qsa_prepare (index queries, compressed keys, ring commit, main K/V) equals
+    the reference kernel run under the Triton interpreter, bit for bit, with the
+    interpreter's truncating bf16 conversion."""
+    d = load("reference_prepare.npz")
+    g, c, eps = _prepare_inputs(d, name)
+    caches = {k: g(k) for k in ("state_cache", "compressed_cache", "main_key_cache",
+                                "main_value_cache")}
+    q = O.qsa_prepare(
+        g("index_qk"), g("positions"), g("q_weight"), g("k_weight"), g("cos_sin"), eps,
+        caches["state_cache"], g("state_slots"), g("state_table"), g("query_start_loc"),
+        g("logical_positions"), caches["compressed_cache"], g("compressed_slots"), g("k_work"),
+        g("main_key"), g("main_value"), caches["main_key_cache"], caches["main_value_cache"],
+        g("main_slots"), num_index_heads=c["heads"], index_head_dim=c["dim"],
+        rotary_dim=c["rotary"], compress_ratio=c["ratio"], rounding="truncate")
+    assert torch.equal(q, torch.from_numpy(d[f"{name}_out_index_q"]))
+    for k, v in caches.items():
+        assert torch.equal(v, torch.from_numpy(d[f"{name}_out_{k}"])), k
