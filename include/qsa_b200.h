@@ -67,7 +67,10 @@ QSA_API int qsa_device_check(void);
  * QSA_DEVICE_ERR_* recorded by kernels whose bounded waits expired.
  */
 QSA_API int qsa_device_error_poll(int32_t* error_bits);
-enum { QSA_DEVICE_ERR_WAIT_TIMEOUT = 1 };
+enum {
+  QSA_DEVICE_ERR_WAIT_TIMEOUT = 1, /* a bounded wait expired */
+  QSA_DEVICE_ERR_OUT_OF_RANGE = 2  /* a slot / position / request outside its buffer was skipped */
+};
 
 /*
  * Top-k selection + expansion.
@@ -157,6 +160,62 @@ QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_he
 QSA_API int qsa_visible_blocks(const int64_t* positions, const int32_t* sequence_lengths,
                                int32_t num_requests, const int32_t* token_to_req, int32_t rows,
                                int32_t ratio, int32_t* visible, void* stream);
+
+/*
+ * Indexer preparation and main K/V cache writes, one launch.
+ * Replaces qsa_prepare / _qsa_prepare_kernel (reference ops/prepare.py:169-228,
+ * kernel :49-166, norm + RoPE :16-46); bound from Python by
+ * qsa_vllm_b200.prepare.qsa_prepare with the reference's signature.
+ *
+ * index_qk: bf16 [num_tokens, >= (num_index_heads + 1) * index_head_dim], row
+ *   stride index_row_stride (elements): the heads' query rows, then the raw key.
+ * positions: int64 (stride positions_stride); q/k_norm_weight: bf16 [dim];
+ * cos_sin_cache: bf16 [cos_sin_rows, rotary_dim] (cosines, then sines; row p
+ *   at p * rotary_dim, as the reference indexes it).
+ * index_q_out: bf16 [num_tokens, num_index_heads, index_head_dim] contiguous:
+ *   RMSNorm(eps) * q weight, then rotate-half RoPE of the first rotary_dim dims,
+ *   with bf16 rounding after each post-norm step.
+ * Key compression, per k_work item (int32 [num_k_work, 2] = (request, work
+ *   item in request); request < 0 = padding): group `work` of the request's
+ *   chunk, the mean of compress_ratio raw keys ending at the group boundary
+ *   (this chunk's keys, or the ring state_cache block state_table[request *
+ *   state_table_stride] for earlier positions), normed with k_norm_weight and
+ *   rotated at the group's first position, stored at
+ *   compressed_slots[boundary token] of compressed_cache [compressed_blocks,
+ *   compressed_page_size, dim].  Work item 0 then writes the chunk's last
+ *   min(query length, state_size) raw keys to state_slots of the ring
+ *   state_cache [state_blocks, state_size, dim].
+ *   query_start_loc: int32 [num_requests + 1]; logical_positions,
+ *   state_slots, compressed_slots: int64 [num_tokens].
+ * Main K/V: main_key / main_value bf16 [num_tokens, num_main_kv_heads,
+ *   main_head_dim] to main_slots (int64) of the paged caches [main_blocks,
+ *   main_page_size, num_main_kv_heads, main_head_dim]; all strides in elements.
+ * Slots < 0 are skipped.  Out-of-range slots, positions or requests (which the
+ * reference would access out of bounds) are skipped and set
+ * QSA_DEVICE_ERR_OUT_OF_RANGE in the device error word.
+ * index_head_dim 64 or 128; index rows 4-byte aligned with even strides.
+ */
+QSA_API int qsa_prepare(
+    const void* index_qk, int64_t index_row_stride, int32_t num_tokens, int32_t num_index_heads,
+    int32_t index_head_dim, const int64_t* positions, int64_t positions_stride,
+    const void* q_norm_weight, const void* k_norm_weight, const void* cos_sin_cache,
+    int64_t cos_sin_rows, int32_t rotary_dim, float eps, void* index_q_out, void* state_cache,
+    int64_t state_block_stride, int64_t state_token_stride, int64_t state_blocks,
+    int32_t state_size, const int64_t* state_slots, const int32_t* state_table,
+    int64_t state_table_stride, const int32_t* query_start_loc, int32_t num_requests,
+    const int64_t* logical_positions, void* compressed_cache, int64_t compressed_block_stride,
+    int64_t compressed_token_stride, int64_t compressed_blocks, int32_t compressed_page_size,
+    const int64_t* compressed_slots, const int32_t* k_work, int32_t num_k_work,
+    int32_t compress_ratio, const void* main_key, int64_t main_key_token_stride,
+    int64_t main_key_head_stride, int64_t main_key_dim_stride, const void* main_value,
+    int64_t main_value_token_stride, int64_t main_value_head_stride,
+    int64_t main_value_dim_stride, void* main_key_cache, int64_t main_key_cache_block_stride,
+    int64_t main_key_cache_token_stride, int64_t main_key_cache_head_stride,
+    int64_t main_key_cache_dim_stride, void* main_value_cache,
+    int64_t main_value_cache_block_stride, int64_t main_value_cache_token_stride,
+    int64_t main_value_cache_head_stride, int64_t main_value_cache_dim_stride,
+    int64_t main_blocks, int32_t main_page_size, const int64_t* main_slots,
+    int32_t num_main_kv_heads, int32_t main_head_dim, void* stream);
 
 /*
  * Workspace bytes qsa_sparse_attention needs for these shapes on the current

@@ -44,6 +44,14 @@ SIGNATURES: dict[str, tuple] = {
         _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i32,
         _vp, _i64, _i32, _vp, _i64, _i32, _i32, _vp, _vp,
         _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _vp, _sz, _vp]),
+    "qsa_prepare": (C.c_int, [
+        _vp, _i64, _i32, _i32, _i32, _vp, _i64,
+        _vp, _vp, _vp, _i64, _i32, _f32, _vp,
+        _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp, _i32, _vp,
+        _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _i32,
+        _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
+        _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+        _i64, _i32, _vp, _i32, _i32, _vp]),
     "qsa_sparse_attention_static_scratch": (C.c_int, [
         _vp, _i64, _i64, _i32, _i32, _i32,
         _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _i32, _i32,

@@ -350,6 +350,131 @@ int qsa_visible_blocks(const int64_t* positions, const int32_t* sequence_lengths
   return QSA_OK;
 }
 
+// ---------------------------------------------------------------- prepare
+int qsa_prepare(const void* index_qk, int64_t index_row_stride, int32_t num_tokens,
+                int32_t num_index_heads, int32_t index_head_dim, const int64_t* positions,
+                int64_t positions_stride, const void* q_norm_weight, const void* k_norm_weight,
+                const void* cos_sin_cache, int64_t cos_sin_rows, int32_t rotary_dim, float eps,
+                void* index_q_out, void* state_cache, int64_t state_block_stride,
+                int64_t state_token_stride, int64_t state_blocks, int32_t state_size,
+                const int64_t* state_slots, const int32_t* state_table,
+                int64_t state_table_stride, const int32_t* query_start_loc,
+                int32_t num_requests, const int64_t* logical_positions, void* compressed_cache,
+                int64_t compressed_block_stride, int64_t compressed_token_stride,
+                int64_t compressed_blocks, int32_t compressed_page_size,
+                const int64_t* compressed_slots, const int32_t* k_work, int32_t num_k_work,
+                int32_t compress_ratio, const void* main_key, int64_t main_key_token_stride,
+                int64_t main_key_head_stride, int64_t main_key_dim_stride,
+                const void* main_value, int64_t main_value_token_stride,
+                int64_t main_value_head_stride, int64_t main_value_dim_stride,
+                void* main_key_cache, int64_t main_key_cache_block_stride,
+                int64_t main_key_cache_token_stride, int64_t main_key_cache_head_stride,
+                int64_t main_key_cache_dim_stride, void* main_value_cache,
+                int64_t main_value_cache_block_stride, int64_t main_value_cache_token_stride,
+                int64_t main_value_cache_head_stride, int64_t main_value_cache_dim_stride,
+                int64_t main_blocks, int32_t main_page_size, const int64_t* main_slots,
+                int32_t num_main_kv_heads, int32_t main_head_dim, void* stream) {
+  const char* who = "qsa_prepare";
+  if (num_tokens < 0 || num_k_work < 0 || num_index_heads <= 0 || num_main_kv_heads < 0 ||
+      num_requests < 0)
+    return fail(QSA_ERR_INVALID, "%s: negative or zero sizes", who);
+  if (index_head_dim != 64 && index_head_dim != 128)
+    return fail(QSA_ERR_UNSUPPORTED, "%s: index head dim %d (64 or 128 supported)", who,
+                index_head_dim);
+  if (rotary_dim < 2 || rotary_dim % 2 || rotary_dim > index_head_dim)
+    return fail(QSA_ERR_INVALID, "%s: rotary dim %d must be even and in [2, %d]", who,
+                rotary_dim, index_head_dim);
+  if (compress_ratio <= 0 || state_size <= 0 || compressed_page_size <= 0 ||
+      (num_main_kv_heads > 0 && (main_page_size <= 0 || main_head_dim <= 0)))
+    return fail(QSA_ERR_INVALID, "%s: ratio, ring size and page sizes must be positive", who);
+  if (num_tokens == 0 && num_k_work == 0) return QSA_OK;
+  if (!index_qk || !positions || !q_norm_weight || !k_norm_weight || !cos_sin_cache ||
+      !index_q_out)
+    return fail(QSA_ERR_INVALID, "%s: null index projection / weights / rotary cache", who);
+  if (num_k_work > 0 && (!state_cache || !state_slots || !state_table || !query_start_loc ||
+                         !logical_positions || !compressed_cache || !compressed_slots || !k_work))
+    return fail(QSA_ERR_INVALID, "%s: null compression metadata or cache", who);
+  if (num_main_kv_heads > 0 && num_tokens > 0 &&
+      (!main_key || !main_value || !main_key_cache || !main_value_cache || !main_slots))
+    return fail(QSA_ERR_INVALID, "%s: null main K/V or cache", who);
+  if (index_row_stride < static_cast<int64_t>(num_index_heads + 1) * index_head_dim)
+    return fail(QSA_ERR_INVALID, "%s: index row stride %lld < (heads + 1) * dim", who,
+                (long long)index_row_stride);
+  // rows are read and written as bf16 pairs
+  if (!aligned(index_qk, 4) || index_row_stride % 2 || !aligned(index_q_out, 4) ||
+      (num_k_work > 0 && (!aligned(state_cache, 4) || state_block_stride % 2 ||
+                          state_token_stride % 2 || !aligned(compressed_cache, 4) ||
+                          compressed_block_stride % 2 || compressed_token_stride % 2)))
+    return fail(QSA_ERR_INVALID, "%s: index rows must be 4-byte aligned with even strides", who);
+  PrepareParams p{};
+  p.index_qk = static_cast<const __nv_bfloat16*>(index_qk);
+  p.index_row_stride = index_row_stride;
+  p.num_tokens = num_tokens;
+  p.heads = num_index_heads;
+  p.dim = index_head_dim;
+  p.positions = positions;
+  p.positions_stride = positions_stride;
+  p.q_weight = static_cast<const __nv_bfloat16*>(q_norm_weight);
+  p.k_weight = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin_cache);
+  p.cos_sin_rows = cos_sin_rows;
+  p.rotary = rotary_dim;
+  p.eps = eps;
+  p.index_q_out = static_cast<__nv_bfloat16*>(index_q_out);
+  p.state_cache = static_cast<__nv_bfloat16*>(state_cache);
+  p.state_block_stride = state_block_stride;
+  p.state_token_stride = state_token_stride;
+  p.state_size = state_size;
+  p.state_blocks = state_blocks;
+  p.state_slots = state_slots;
+  p.state_table = state_table;
+  p.state_table_stride = state_table_stride;
+  p.query_start_loc = query_start_loc;
+  p.num_requests = num_requests;
+  p.logical_positions = logical_positions;
+  p.compressed_cache = static_cast<__nv_bfloat16*>(compressed_cache);
+  p.comp_block_stride = compressed_block_stride;
+  p.comp_token_stride = compressed_token_stride;
+  p.comp_page = compressed_page_size;
+  p.comp_blocks = compressed_blocks;
+  p.compressed_slots = compressed_slots;
+  p.k_work = k_work;
+  p.num_k_work = num_k_work;
+  p.ratio = compress_ratio;
+  p.main_key = static_cast<const __nv_bfloat16*>(main_key);
+  p.main_value = static_cast<const __nv_bfloat16*>(main_value);
+  p.main_key_cache = static_cast<__nv_bfloat16*>(main_key_cache);
+  p.main_value_cache = static_cast<__nv_bfloat16*>(main_value_cache);
+  const int64_t mk[3] = {main_key_token_stride, main_key_head_stride, main_key_dim_stride};
+  const int64_t mv[3] = {main_value_token_stride, main_value_head_stride, main_value_dim_stride};
+  const int64_t kc[4] = {main_key_cache_block_stride, main_key_cache_token_stride,
+                         main_key_cache_head_stride, main_key_cache_dim_stride};
+  const int64_t vc[4] = {main_value_cache_block_stride, main_value_cache_token_stride,
+                         main_value_cache_head_stride, main_value_cache_dim_stride};
+  bool vec = main_head_dim % 8 == 0 && aligned(main_key, 16) && aligned(main_value, 16) &&
+             aligned(main_key_cache, 16) && aligned(main_value_cache, 16);
+  for (int i = 0; i < 3; ++i) {
+    p.mk_stride[i] = mk[i];
+    p.mv_stride[i] = mv[i];
+    vec = vec && (i == 2 ? mk[i] == 1 && mv[i] == 1 : mk[i] % 8 == 0 && mv[i] % 8 == 0);
+  }
+  for (int i = 0; i < 4; ++i) {
+    p.kc_stride[i] = kc[i];
+    p.vc_stride[i] = vc[i];
+    vec = vec && (i == 3 ? kc[i] == 1 && vc[i] == 1 : kc[i] % 8 == 0 && vc[i] % 8 == 0);
+  }
+  p.main_slots = main_slots;
+  p.kv_heads = num_main_kv_heads;
+  p.main_dim = main_head_dim;
+  p.main_page = main_page_size;
+  p.main_blocks = main_blocks;
+  p.main_vec = vec ? 1 : 0;
+  p.err = device_error_word();
+  cudaError_t e = launch_prepare(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
 // -------------------------------------------------------------- attention
 size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
                                             int32_t num_kv_heads, int32_t head_dim,

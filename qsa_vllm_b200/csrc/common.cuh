@@ -15,6 +15,8 @@ namespace qsa {
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 constexpr int kDeviceErrWaitTimeout = 1;
+// An index (slot, page, position, request) outside its buffer: the access was skipped.
+constexpr int kDeviceErrOutOfRange = 2;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -138,6 +138,53 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
                         int use_decode_kernel);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
 
+// --------------------------------------------------------------- prepare
+struct PrepareParams {
+  // index projection [tokens, (heads + 1) * dim]: heads query rows, then the raw key
+  const __nv_bfloat16* index_qk;
+  int64_t index_row_stride;
+  int num_tokens, heads, dim;
+  const int64_t* positions;
+  int64_t positions_stride;
+  const __nv_bfloat16 *q_weight, *k_weight;
+  const __nv_bfloat16* cos_sin;  // [cos_sin_rows, rotary]: cosines, then sines
+  int64_t cos_sin_rows;
+  int rotary;
+  float eps;
+  __nv_bfloat16* index_q_out;    // [tokens, heads, dim] contiguous
+  // raw-key ring: [state_blocks, state_size, dim]
+  __nv_bfloat16* state_cache;
+  int64_t state_block_stride, state_token_stride;
+  int state_size;
+  int64_t state_blocks;
+  const int64_t* state_slots;
+  const int32_t* state_table;
+  int64_t state_table_stride;
+  const int32_t* query_start_loc;
+  int num_requests;
+  const int64_t* logical_positions;
+  // compressed keys: [comp_blocks, comp_page, dim]
+  __nv_bfloat16* compressed_cache;
+  int64_t comp_block_stride, comp_token_stride;
+  int comp_page;
+  int64_t comp_blocks;
+  const int64_t* compressed_slots;
+  const int32_t* k_work;  // [num_k_work, 2]: (request, work item in request)
+  int num_k_work, ratio;
+  // main K/V rows [tokens, kv_heads, main_dim] into paged caches
+  // [main_blocks, main_page, kv_heads, main_dim]
+  const __nv_bfloat16 *main_key, *main_value;
+  int64_t mk_stride[3], mv_stride[3];
+  __nv_bfloat16 *main_key_cache, *main_value_cache;
+  int64_t kc_stride[4], vc_stride[4];
+  const int64_t* main_slots;
+  int kv_heads, main_dim, main_page;
+  int64_t main_blocks;
+  int main_vec;   // unit dim strides and 16-byte aligned rows: 16-byte copies
+  int* err;
+};
+cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t stream);
+
 int num_sms();
 // Counts `n` kernel launches of this library when `e` reports success (the
 // host-side count read by qsa_kernel_launches); returns `e`.

@@ -3,7 +3,9 @@
     python -m qsa_vllm_b200.profile_kernels --kernel attention --config cfg2_32k \
         --batch 16 --iters 3 [--contiguous-tables] [--time]
 
-``--kernel``: ``indexer`` | ``topk`` | ``attention`` | ``step`` (all three).
+``--kernel``: ``indexer`` | ``topk`` | ``attention`` | ``step`` (all three) |
+``prepare`` (index-query norm/RoPE, key compression, cache writes) | ``layer``
+(``prepare`` then ``step``, the reference layer's forward).
 Inputs are the synthetic workload of ``--config`` with ``--batch`` rows (the
 same per-row shapes as the benchmark, a smaller device footprint for ncu
 captures).  ``--contiguous-tables`` replaces the random block tables with the
@@ -22,14 +24,15 @@ import torch
 
 from .indexer import compute_visible_blocks, indexer_scores, select_paged_tokens
 from .qsa import qsa_sparse_paged_attention
-from .synthetic import make_workload
+from .prepare import qsa_prepare
+from .synthetic import make_prepare_inputs, make_workload
 from .topk import topk_expand
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", default="attention",
-                    choices=["indexer", "topk", "attention", "step"])
+                    choices=["indexer", "topk", "attention", "step", "prepare", "layer"])
     ap.add_argument("--config", default="cfg2_32k")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--iters", type=int, default=3)
@@ -93,10 +96,19 @@ def main() -> None:
             weights=w.index_weights, scale=w.index_scale, visible_blocks=given)
         run_attention()
 
+    prep = make_prepare_inputs(w) if a.kernel in ("prepare", "layer") else None
+
+    def run_prepare():
+        qsa_prepare(**prep)
+
+    def run_layer():
+        run_prepare()
+        run_step()
+
     run_indexer()
     run_topk()
     fn = {"indexer": run_indexer, "topk": run_topk, "attention": run_attention,
-          "step": run_step}[a.kernel]
+          "step": run_step, "prepare": run_prepare, "layer": run_layer}[a.kernel]
     for _ in range(a.warmup):
         fn()
     torch.cuda.synchronize()

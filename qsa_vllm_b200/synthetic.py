@@ -191,4 +191,74 @@ def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
                "max_query_len": int(q_lens.max())})
 
 
-__all__ = ["CONFIGS", "SyntheticQSA", "make_workload"]
+def rope_cache(max_position: int, rotary_dim: int, theta: float, device) -> torch.Tensor:
+    """bf16 [max_position, rotary_dim]: cos(p * theta^(-2i/rotary)) for the
+    rotary_dim/2 channels, then the sines (the layout ops/normalization.py:18-23
+    builds)."""
+    inv = theta ** (-torch.arange(0, rotary_dim, 2, dtype=torch.float32) / rotary_dim)
+    phase = torch.outer(torch.arange(max_position, dtype=torch.float32), inv)
+    return torch.cat((phase.cos(), phase.sin()), -1).to(torch.bfloat16).to(device)
+
+
+def make_prepare_inputs(w: SyntheticQSA, *, seed: int = 0, state_size: int = 64,
+                        rotary_dim: int | None = None, theta: float = 1e7) -> dict:
+    """Keyword arguments of ``qsa_vllm_b200.prepare.qsa_prepare`` for the step of
+    ``w``: a fresh index projection (bf16 N(0,1), ``[rows, (H_i + 1) * d_i]``),
+    main K/V rows written into ``w``'s paged pool at each token's slot, the
+    compressed key of every group that ends in this step written into ``w``'s
+    index-key cache (slot from its index table), and one raw-key ring of
+    ``state_size`` rows per request.  Metadata is built on the host, as a
+    scheduler does, then moved to the device."""
+    dev = w.q.device
+    hi, di = w.index_q.shape[1], w.index_q.shape[2]
+    hkv, d = w.kv.shape[2], w.d
+    r, page = w.ratio, w.page_size
+    rows = w.rows
+    rotary_dim = di if rotary_dim is None else rotary_dim
+    pos = w.positions.cpu()
+    req = w.token_to_req.cpu().long()
+    qsl = w.query_start_loc.cpu()
+    table = w.block_table.cpu().long()
+    itable = w.index_table.cpu().long()
+    ipage = w.index_cache.shape[1]
+    B = qsl.numel() - 1
+    main_slots = table[req, pos // page] * page + pos % page
+    blk = pos // r
+    comp_slots = torch.where((pos + 1) % r == 0,
+                             itable[req, (blk // ipage).clamp(max=itable.shape[1] - 1)] * ipage
+                             + blk % ipage, torch.full_like(pos, -1))
+    state_slots = req * state_size + pos % state_size
+    work = []
+    for b in range(B):
+        q0, q1 = int(qsl[b]), int(qsl[b + 1])
+        if q1 <= q0:
+            continue
+        end = int(pos[q1 - 1])
+        start = end - (q1 - q0) + 1
+        groups = (end + 1) // r - start // r
+        work += [[b, i] for i in range(max(groups, 1))]
+    g = torch.Generator(device=dev).manual_seed(seed + 7)
+
+    def randn(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    from types import SimpleNamespace
+    raw = SimpleNamespace(slot_mapping=state_slots.to(dev),
+                          block_table=torch.arange(B, dtype=torch.int32, device=dev)[:, None],
+                          query_start_loc=w.query_start_loc, logical_positions=w.positions)
+    comp = SimpleNamespace(slot_mapping=comp_slots.to(dev),
+                           k_work_metadata=torch.tensor(work, dtype=torch.int32,
+                                                        device=dev).reshape(-1, 2))
+    return dict(
+        index_qk=randn(rows, (hi + 1) * di), positions=w.positions,
+        q_norm_weight=randn(di, scale=0.1) + 1, k_norm_weight=randn(di, scale=0.1) + 1,
+        cos_sin_cache=rope_cache(w.max_seq_len + 1, rotary_dim, theta, dev), eps=1e-6,
+        raw_metadata=raw, compressed_metadata=comp,
+        state_cache=randn(B, state_size, di), compressed_cache=w.index_cache,
+        main_key=randn(rows, hkv, d), main_value=randn(rows, hkv, d),
+        main_key_cache=w.k_cache, main_value_cache=w.v_cache,
+        main_slots=main_slots.to(dev), num_index_heads=hi, index_head_dim=di,
+        rotary_dim=rotary_dim, compress_ratio=r)
+
+
+__all__ = ["CONFIGS", "SyntheticQSA", "make_prepare_inputs", "make_workload", "rope_cache"]

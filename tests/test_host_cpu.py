@@ -75,6 +75,66 @@ def test_argument_errors_are_reported_not_launched():
         _lib.check(1, "probe")
 
 
+def _prepare_args(**over):
+    """qsa_prepare's 58 C arguments (null pointers, unit strides), by name."""
+    names = ("index_qk index_row_stride num_tokens num_index_heads index_head_dim positions "
+             "positions_stride q_norm_weight k_norm_weight cos_sin_cache cos_sin_rows rotary_dim "
+             "eps index_q_out state_cache state_block_stride state_token_stride state_blocks "
+             "state_size state_slots state_table state_table_stride query_start_loc num_requests "
+             "logical_positions compressed_cache compressed_block_stride compressed_token_stride "
+             "compressed_blocks compressed_page_size compressed_slots k_work num_k_work "
+             "compress_ratio main_key mk0 mk1 mk2 main_value mv0 mv1 mv2 main_key_cache kc0 kc1 "
+             "kc2 kc3 main_value_cache vc0 vc1 vc2 vc3 main_blocks main_page_size main_slots "
+             "num_main_kv_heads main_head_dim stream").split()
+    assert len(names) == 58
+    vals = dict.fromkeys(names, None)
+    vals.update(index_row_stride=576, num_tokens=4, num_index_heads=8, index_head_dim=64,
+                positions_stride=1, cos_sin_rows=4096, rotary_dim=64, eps=1e-6,
+                state_block_stride=8192, state_token_stride=64, state_blocks=4, state_size=128,
+                state_table_stride=1, num_requests=1, compressed_block_stride=4096,
+                compressed_token_stride=64, compressed_blocks=4, compressed_page_size=64,
+                num_k_work=1, compress_ratio=4, mk0=512, mk1=128, mk2=1, mv0=512, mv1=128,
+                mv2=1, kc0=32768, kc1=512, kc2=128, kc3=1, vc0=32768, vc1=512, vc2=128, vc3=1,
+                main_blocks=4, main_page_size=64, num_main_kv_heads=4, main_head_dim=128)
+    vals.update(over)
+    return [vals[n] for n in names]
+
+
+def test_prepare_argument_errors_are_reported_not_launched():
+    from qsa_vllm_b200 import _lib
+    lib = _lib.load_library()
+    # nothing to do: no device access
+    assert lib.qsa_prepare(*_prepare_args(num_tokens=0, num_k_work=0)) == 0
+    assert lib.qsa_prepare(*_prepare_args(index_head_dim=96)) == 2
+    assert b"index head dim" in lib.qsa_last_error()
+    assert lib.qsa_prepare(*_prepare_args(rotary_dim=33)) == 1
+    assert b"rotary" in lib.qsa_last_error()
+    assert lib.qsa_prepare(*_prepare_args(compress_ratio=0)) == 1
+    # a real launch needs the projection, weights and caches
+    assert lib.qsa_prepare(*_prepare_args()) == 1
+    assert b"null" in lib.qsa_last_error()
+
+
+def test_prepare_fails_loudly_without_a_gpu():
+    from types import SimpleNamespace
+
+    from qsa_vllm_b200 import _lib
+    from qsa_vllm_b200.prepare import qsa_prepare
+    bf = torch.bfloat16
+    i64 = torch.zeros(4, dtype=torch.int64)
+    raw = SimpleNamespace(slot_mapping=i64, block_table=torch.zeros(1, 1, dtype=torch.int32),
+                          query_start_loc=torch.tensor([0, 4], dtype=torch.int32),
+                          logical_positions=i64)
+    comp = SimpleNamespace(slot_mapping=i64, k_work_metadata=torch.zeros(1, 2, dtype=torch.int32))
+    with pytest.raises(_lib.QSAError):
+        qsa_prepare(torch.zeros(4, 576, dtype=bf), i64, torch.ones(64, dtype=bf),
+                    torch.ones(64, dtype=bf), torch.zeros(16, 64, dtype=bf), 1e-6, raw, comp,
+                    torch.zeros(2, 8, 64, dtype=bf), torch.zeros(2, 16, 64, dtype=bf),
+                    torch.zeros(4, 2, 128, dtype=bf), torch.zeros(4, 2, 128, dtype=bf),
+                    torch.zeros(2, 16, 2, 128, dtype=bf), torch.zeros(2, 16, 2, 128, dtype=bf),
+                    i64, num_index_heads=8, index_head_dim=64, rotary_dim=64, compress_ratio=4)
+
+
 def test_attention_workspace_query_is_deterministic():
     from qsa_vllm_b200.qsa import attention_workspace_bytes
     a = attention_workspace_bytes(64, 32, 4, 128, 2051, True)
