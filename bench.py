@@ -283,8 +283,7 @@ def main() -> None:
     def step():
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
-            w.token_topk, w.ratio, idx_buf, query_start_loc=w.query_start_loc, max_query_len=1,
-            max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            w.token_topk, w.ratio, idx_buf, **w.select_kwargs(),
             visible_blocks=w.visible_blocks,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt_buf,
             weights=w.index_weights, scale=w.index_scale)
@@ -396,8 +395,7 @@ def main() -> None:
         dev_meta.copy_(host_meta, non_blocking=True)
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
-            w.token_topk, w.ratio, idx_buf, query_start_loc=w.query_start_loc, max_query_len=1,
-            max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+            w.token_topk, w.ratio, idx_buf, **w.select_kwargs(),
             visible_blocks=w.visible_blocks,
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt_buf,
             weights=w.index_weights, scale=w.index_scale)

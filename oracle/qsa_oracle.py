@@ -445,7 +445,8 @@ def decode_step(w, *, round_p: bool = True):
     vis = visible_blocks(w.positions, w.seq_lens, w.token_to_req, w.ratio)
     columns = w.index_table.shape[1] * w.index_cache.shape[1]
     logits = indexer_scores(w.index_q, w.index_cache, w.index_table, vis, columns,
-                            decode_query_len=1, weights=w.index_weights,
+                            decode_query_len=getattr(w, "decode_query_len", 1),
+                            weights=w.index_weights,
                             scale=w.index_scale)
     idx, counts = topk_expand(logits, vis, w.positions, w.seq_lens, w.token_to_req,
                               w.block_table, w.token_topk + w.ratio - 1, w.ratio,

@@ -64,8 +64,8 @@ def main() -> None:
     out = torch.empty_like(w.q)
 
     # decode rows: one page-table row per request; prefill: packed rows
-    prefill = {} if w.is_decode else dict(query_start_loc=w.query_start_loc,
-                                          max_query_len=w.max_query_len)
+    prefill = (dict(decode_query_len=w.decode_query_len) if w.is_decode else
+               dict(query_start_loc=w.query_start_loc, max_query_len=w.max_query_len))
 
     def run_indexer():
         indexer_scores(w.index_q, w.index_cache, w.index_table, vis, logits,
@@ -86,12 +86,9 @@ def main() -> None:
         # layer), unless --visible-kernel recomputes them inside the step
         given = (compute_visible_blocks(w.positions, w.seq_lens, w.token_to_req, r)
                  if a.visible_kernel else vis)
-        decodes = rows if w.is_decode else 0   # prefill configs: packed prefill rows only
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
-            w.token_topk, r, idx, query_start_loc=w.query_start_loc,
-            max_query_len=1 if w.is_decode else w.max_query_len,
-            max_seq_len=w.max_seq_len, num_decodes=decodes, num_decode_tokens=decodes,
+            w.token_topk, r, idx, **w.select_kwargs(),
             main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=cnt,
             weights=w.index_weights, scale=w.index_scale, visible_blocks=given)
         run_attention()

@@ -11,7 +11,8 @@ Layouts match what the reference plugin receives from vLLM:
     ``v_cache`` are the two halves of the last dim (backend.py:148-153);
   * index-key cache: bf16 ``[num_index_blocks, index_page, 1, d_i]`` (one
     compressed key per ``ratio`` tokens) with its own block table;
-  * decode rows are the last token of each request: position = seq_len - 1.
+  * decode rows are the last token of each request: position = seq_len - 1
+    (the last ``dql`` tokens for multi-token decode).
 """
 
 from __future__ import annotations
@@ -32,6 +33,12 @@ CONFIGS: dict[str, dict] = {
                      token_topk=2048, ratio=4),
     "cfg3": dict(batch=8, seq_len=131072, hq=32, hkv=4, d=128, hi=8, di=64, page=64,
                  token_topk=2048, ratio=4),
+    # variants of the headline decode point: per-token index keys (ratio 1), and
+    # multi-token (MTP) decode with two query rows per request
+    "cfg2_32k_r1": dict(batch=64, seq_len=32768, hq=32, hkv=4, d=128, hi=8, di=64, page=64,
+                        token_topk=2048, ratio=1),
+    "cfg2_32k_mtp2": dict(batch=64, seq_len=32768, hq=32, hkv=4, d=128, hi=8, di=64, page=64,
+                          token_topk=2048, ratio=4, dql=2),
 }
 
 
@@ -82,6 +89,22 @@ class SyntheticQSA:
     @property
     def max_query_len(self) -> int:
         return self.extra["max_query_len"]
+
+    @property
+    def decode_query_len(self) -> int:
+        return self.extra.get("decode_query_len", 1)
+
+    def select_kwargs(self) -> dict:
+        """Batch-shape keywords of ``select_paged_tokens`` for this step: every
+        row a decode row (``decode_query_len`` per request), or every row a
+        packed prefill row."""
+        if self.is_decode:
+            dql = self.decode_query_len
+            return dict(query_start_loc=self.query_start_loc, max_query_len=dql,
+                        max_seq_len=self.max_seq_len, num_decodes=self.rows // dql,
+                        num_decode_tokens=self.rows, decode_query_len=dql)
+        return dict(query_start_loc=self.query_start_loc, max_query_len=self.max_query_len,
+                    max_seq_len=self.max_seq_len)
 
     def shard_heads(self, tp_size: int, tp_rank: int) -> "SyntheticQSA":
         """This rank's view under head (tensor-parallel) sharding: query heads and
@@ -140,8 +163,9 @@ def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
         seq_lens = torch.full((B,), int(sl), dtype=torch.int32)
     new = cfg.get("new_tokens")
     is_decode = new is None
+    dql = int(cfg.get("dql", 1))
     if is_decode:
-        q_lens = torch.ones(B, dtype=torch.int32)
+        q_lens = torch.full((B,), dql, dtype=torch.int32)
     else:
         q_lens = torch.full((B,), int(new), dtype=torch.int32)
     qsl = torch.zeros(B + 1, dtype=torch.int32)
@@ -188,7 +212,7 @@ def make_workload(name: str = "cfg2_32k", *, device="cuda", seed: int = 0,
         index_scale=di ** -0.5, index_cache=index_cache, index_table=index_table.to(device),
         is_decode=is_decode,
         extra={"config": cfg, "max_seq_len": int(seq_lens.max()),
-               "max_query_len": int(q_lens.max())})
+               "max_query_len": int(q_lens.max()), "decode_query_len": dql})
 
 
 def rope_cache(max_position: int, rotary_dim: int, theta: float, device) -> torch.Tensor:

@@ -391,8 +391,7 @@ def _decode_step(w, dev):
     counts = torch.empty(rows, dtype=torch.int32, device=dev)
     select_paged_tokens(
         w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
-        w.token_topk, w.ratio, out_idx, query_start_loc=w.query_start_loc, max_query_len=1,
-        max_seq_len=w.max_seq_len, num_decodes=rows, num_decode_tokens=rows,
+        w.token_topk, w.ratio, out_idx, **w.select_kwargs(),
         main_block_table=w.block_table, main_page_size=w.page_size, valid_counts_out=counts,
         weights=w.index_weights, scale=w.index_scale)
     out = torch.empty_like(w.q)
@@ -410,12 +409,13 @@ def _check_decode_rows(w, dev, out_idx, counts, out, rows_to_check):
     vis = O.visible_blocks(w.positions.cpu(), w.seq_lens.cpu(), w.token_to_req.cpu(), w.ratio)
     cols = w.index_table.shape[1] * w.index_cache.shape[1]
     logits = torch.zeros(w.rows, cols, device=dev)
+    dql = w.decode_query_len
     indexer_scores(w.index_q, w.index_cache, w.index_table, vis.to(dev), logits,
-                   weights=w.index_weights, scale=w.index_scale)
+                   decode_query_len=dql, weights=w.index_weights, scale=w.index_scale)
     gl = logits.cpu()
     sel = torch.tensor(rows_to_check)
     ref_l = O.indexer_scores(w.index_q.cpu()[sel], w.index_cache.cpu(),
-                             w.index_table.cpu()[sel], vis[sel], cols,
+                             w.index_table.cpu()[sel // dql], vis[sel], cols,
                              weights=w.index_weights.cpu()[sel], scale=w.index_scale)
     for i, r in enumerate(rows_to_check):
         n = int(vis[r])
@@ -471,6 +471,26 @@ def test_decode_step_cfg3_long_context(dev):
     w = make_workload("cfg3", device=dev, seed=2)
     out_idx, counts, out = _decode_step(w, dev)
     _check_decode_rows(w, dev, out_idx, counts, out, [0, 7])
+
+
+def test_decode_step_ratio1(dev):
+    """Per-token index keys (compress ratio 1): 32768-wide score rows, the
+    clustered top-k, no causal tail."""
+    from qsa_vllm_b200.synthetic import make_workload
+    w = make_workload("cfg2_32k_r1", device=dev, seed=4, batch=8)
+    out_idx, counts, out = _decode_step(w, dev)
+    _check_decode_rows(w, dev, out_idx, counts, out, [0, 5])
+    assert bool((counts == w.token_topk).all())
+
+
+def test_decode_step_mtp2(dev):
+    """Multi-token decode: two query rows per request share its page-table row;
+    the second row sees one more token (and possibly one more block)."""
+    from qsa_vllm_b200.synthetic import make_workload
+    w = make_workload("cfg2_32k_mtp2", device=dev, seed=5, batch=8, seq_len=(8190, 8195))
+    assert w.rows == 16 and w.decode_query_len == 2
+    out_idx, counts, out = _decode_step(w, dev)
+    _check_decode_rows(w, dev, out_idx, counts, out, [0, 1, 14, 15])
 
 
 def test_prefill_step_cfg1(dev):
