@@ -59,6 +59,14 @@ QSA_API const char* qsa_version(void);
  * counterpart in the reference; used by benchmarks to report launches per step.
  */
 QSA_API uint64_t qsa_kernel_launches(void);
+/*
+ * Measurement hook, no counterpart in the reference: while set (non-NULL),
+ * qsa_sparse_attention* records the cudaEvent_t `before` on its stream right
+ * before launching the main attention kernel and `after` right after it (before
+ * the split merge), so a caller can time that kernel alone with
+ * cudaEventElapsedTime.  Per host thread; NULL, NULL clears it.
+ */
+QSA_API int qsa_set_attention_timing_events(void* before, void* after);
 /* QSA_OK when the current device is sm_100; QSA_ERR_DEVICE otherwise. */
 QSA_API int qsa_device_check(void);
 /*

@@ -27,6 +27,7 @@ SIGNATURES: dict[str, tuple] = {
     "qsa_last_error": (C.c_char_p, []),
     "qsa_version": (C.c_char_p, []),
     "qsa_kernel_launches": (C.c_uint64, []),
+    "qsa_set_attention_timing_events": (C.c_int, [_vp, _vp]),
     "qsa_device_check": (C.c_int, []),
     "qsa_device_error_poll": (C.c_int, [C.POINTER(_i32)]),
     "qsa_topk_expand": (C.c_int, [
@@ -119,6 +120,21 @@ def device_error_poll() -> int:
 
 def version() -> str:
     return load_library().qsa_version().decode()
+
+
+def set_attention_timing_events(before, after) -> None:
+    """Have the library record two ``torch.cuda.Event``s around the main
+    attention kernel of later attention calls on this thread (None, None
+    clears)."""
+    lib = load_library()
+
+    def handle(e):
+        if e is None:
+            return None
+        if not e.cuda_event:   # torch creates the CUDA event at its first record
+            e.record()
+        return e.cuda_event
+    check(lib.qsa_set_attention_timing_events(handle(before), handle(after)), "timing events")
 
 
 def kernel_launches() -> int:

@@ -653,9 +653,11 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
                                 static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int grid = p.sk_ctas;
+  record_attention_event(0, stream);
   e = count_launches(
       launch_kernel(attention_kernel<D, NT, HB>, dim3(grid), dim3(kThreads), smem, stream, 1, p));
   if (e != cudaSuccess) return e;
+  record_attention_event(1, stream);
   return count_launches(launch_kernel(
       merge_kernel<D>, dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads),
       dim3(kMergeHeads * 32), 0, stream, 1, p));

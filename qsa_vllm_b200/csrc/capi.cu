@@ -73,6 +73,19 @@ int set_last_error(int status, const char* fmt, ...) {
 }
 
 std::atomic<uint64_t> g_launches{0};
+thread_local cudaEvent_t g_attention_events[2] = {nullptr, nullptr};
+
+void record_attention_event(int which, cudaStream_t stream) {
+  cudaEvent_t ev = g_attention_events[which];
+  if (ev == nullptr) return;
+  // under stream capture the record becomes an event node of the graph, so
+  // graph replays time the kernel too
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(stream, &cap);
+  cudaEventRecordWithFlags(ev, stream,
+                           cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
+                                                                : cudaEventRecordDefault);
+}
 
 cudaError_t count_launches(cudaError_t e, int n) {
   if (e == cudaSuccess) g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed);
@@ -132,6 +145,12 @@ const char* qsa_last_error(void) { return g_last_error; }
 const char* qsa_version(void) { return "qsa_b200 0.1.0 (sm_100a)"; }
 
 uint64_t qsa_kernel_launches(void) { return qsa::g_launches.load(std::memory_order_relaxed); }
+
+int qsa_set_attention_timing_events(void* before, void* after) {
+  qsa::g_attention_events[0] = static_cast<cudaEvent_t>(before);
+  qsa::g_attention_events[1] = static_cast<cudaEvent_t>(after);
+  return QSA_OK;
+}
 
 int qsa_device_check(void) {
   int dev = 0;

@@ -186,6 +186,9 @@ struct PrepareParams {
 cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t stream);
 
 int num_sms();
+// Records this host thread's attention timing event `which` (0: before the
+// main attention kernel, 1: after it) on `stream`, when one is set.
+void record_attention_event(int which, cudaStream_t stream);
 // Counts `n` kernel launches of this library when `e` reports success (the
 // host-side count read by qsa_kernel_launches); returns `e`.
 cudaError_t count_launches(cudaError_t e, int n = 1);
