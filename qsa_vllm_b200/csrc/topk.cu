@@ -7,9 +7,11 @@
 // length is <= K emit 0..length-1.
 //
 // Design (B200), latency first (a decode step selects over only ~2-8 MB):
-//   * one CTA of 1024 threads per row slice; each thread keeps its keys (8,
-//     or 32 for very wide rows) in REGISTERS after one coalesced 16-byte load
-//     pass from HBM, so every radix pass re-reads registers, not memory;
+//   * one CTA per row slice, sized to the row: 256 or 512 threads for rows of
+//     up to 2048 / 4096 keys (prefill rows; several CTAs share an SM), 1024
+//     threads above; each thread keeps its keys (8, or 32 for very wide rows)
+//     in REGISTERS after one coalesced 16-byte load pass from HBM, so every
+//     radix pass re-reads registers, not memory;
 //   * radix select, most-significant digit first, in digits of up to 11
 //     bits below the high bits shared by every key of the row (found from the
 //     row's min and max key first: scores of similar magnitude share sign and
@@ -37,8 +39,7 @@ namespace cg = cooperative_groups;
 namespace qsa {
 namespace {
 
-constexpr int kThreads = 1024;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 1024;  // widest CTA (rows above 4096 keys and clusters)
 constexpr int kBins = 2048;
 constexpr int kMaxCluster = 16;
 constexpr int kMaxSelBytes = 192 * 1024;  // selected ids of one CTA: up to 49152 blocks
@@ -117,12 +118,13 @@ __device__ __forceinline__ void write_rank(const TopkParams& p, const RowMeta& m
   store_block(p, m, out_row, rank, block, ph);
 }
 
-// Causal tail, -1 fill and valid count (topk.cu:152-162).
+// Causal tail, -1 fill and valid count (topk.cu:152-162).  T threads.
+template <int T>
 __device__ __forceinline__ void finish_row(const TopkParams& p, const RowMeta& m,
                                            int32_t* out_row, int row) {
   const int expanded = m.complete * p.ratio;
   for (int col = max(expanded, 0) + static_cast<int>(threadIdx.x); col < p.out_width;
-       col += kThreads) {
+       col += T) {
     const int off = col - expanded;
     out_row[static_cast<int64_t>(col) * p.out_col_stride] =
         (off < m.tail_count && off < p.ratio - 1) ? map_token(p, m, m.tail_start + off) : -1;
@@ -139,8 +141,8 @@ __device__ __forceinline__ void hist_add(int* hist, bool valid, uint32_t bin) {
 
 // Block-wide exclusive prefix sums of NC counters per thread in one round
 // (one barrier pair): ex[c] = sum of v[c] over lower threads, tot[c] = sum
-// over the block.  `tmp` holds kWarps * NC ints.
-template <int NC>
+// over the block of W warps.  `tmp` holds W * NC ints.
+template <int NC, int W>
 __device__ __forceinline__ void block_scan_multi(const int (&v)[NC], int (&ex)[NC],
                                                  int (&tot)[NC], int* tmp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -163,26 +165,28 @@ __device__ __forceinline__ void block_scan_multi(const int (&v)[NC], int (&ex)[N
   if (warp == 0) {
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      int w = lane < kWarps ? tmp[lane * NC + c] : 0;
+      int w = lane < W ? tmp[lane * NC + c] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, w, o);
         if (lane >= o) w += y;
       }
       __syncwarp();
-      if (lane < kWarps) tmp[lane * NC + c] = w;  // inclusive warp prefix
+      if (lane < W) tmp[lane * NC + c] = w;  // inclusive warp prefix
     }
   }
   __syncthreads();
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    tot[c] = tmp[(kWarps - 1) * NC + c];
+    tot[c] = tmp[(W - 1) * NC + c];
     ex[c] = (warp == 0 ? 0 : tmp[(warp - 1) * NC + c]) + x[c] - v[c];
   }
   __syncthreads();
 }
 
-// Block-wide exclusive prefix sum of one int per thread; also returns the total.
+// Block-wide (W warps) exclusive prefix sum of one int per thread; also
+// returns the total.
+template <int W>
 __device__ __forceinline__ int block_exclusive_sum(int v, int* warp_tmp, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -194,28 +198,29 @@ __device__ __forceinline__ int block_exclusive_sum(int v, int* warp_tmp, int& to
   if (lane == 31) warp_tmp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = lane < kWarps ? warp_tmp[lane] : 0;
+    int w = lane < W ? warp_tmp[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    if (lane < kWarps) warp_tmp[lane] = w;  // inclusive warp prefix
+    if (lane < W) warp_tmp[lane] = w;  // inclusive warp prefix
   }
   __syncthreads();
-  total = warp_tmp[kWarps - 1];
+  total = warp_tmp[W - 1];
   const int before = warp == 0 ? 0 : warp_tmp[warp - 1];
   const int result = before + x - v;
   __syncthreads();
   return result;
 }
 
-// V keys per thread; the slice of a CTA is kThreads * V keys, stored as
-// V/4 chunks of kThreads float4 (thread t holds keys 4*(c*kThreads+t)+0..3).
-template <int V>
-__global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
+// T threads, V keys per thread; the slice of a CTA is T * V keys, stored as
+// V/4 chunks of T float4 (thread t holds keys 4*(c*T+t)+0..3).
+template <int T, int V>
+__global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
   constexpr int kChunks = V / 4;
-  constexpr int kChunkKeys = 4 * kThreads;
+  constexpr int kWarps = T / 32;
+  constexpr int kPer = kBins / T > 0 ? kBins / T : 1;  // most bins one thread ranks
   extern __shared__ int sel[];  // selected column ids of this CTA, by rank (topk entries)
   __shared__ int hist[2][kBins];
   __shared__ int warp_tmp[kWarps * kChunks * 2];
@@ -245,9 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   if (length <= topk) {
     // Every column is selected (topk.cu:187-191); no score is read.
     const int n = p.expand ? max(m.complete, 0) : topk;
-    for (int j = crank * kThreads + tid; j < n; j += C * kThreads)
+    for (int j = crank * T + tid; j < n; j += C * T)
       write_rank(p, m, out_row, j, j < length ? j : -1);
-    if (crank == 0 && p.expand) finish_row(p, m, out_row, row);
+    if (crank == 0 && p.expand) finish_row<T>(p, m, out_row, row);
     return;  // uniform across the cluster: no CTA reaches a cluster barrier
   }
 
@@ -255,12 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   const int per = ((length + C - 1) / C + 3) & ~3;
   const int begin = min(crank * per, length);
   const int n = min(begin + per, length) - begin;
-  for (int b = tid; b < 2 * kBins; b += kThreads) (&hist[0][0])[b] = 0;
+  for (int b = tid; b < 2 * kBins; b += T) (&hist[0][0])[b] = 0;
   const float* src = p.scores + static_cast<int64_t>(row) * p.score_row_stride + begin;
   uint32_t key[V];
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
-    const int e = 4 * (c * kThreads + tid);
+    const int e = 4 * (c * T + tid);
     if (p.vec4 && e + 3 < n) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + e));
       key[4 * c] = v.x;
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
       for (int j = 0; j < 4; ++j) key[4 * c + j] = e + j < n ? __float_as_uint(src[e + j]) : 0u;
     }
   }
-  auto valid_at = [&](int i) { return 4 * ((i / 4) * kThreads + tid) + (i % 4) < n; };
+  auto valid_at = [&](int i) { return 4 * ((i / 4) * T + tid) + (i % 4) < n; };
 
   // ---- min and max key of the row: their common high bits are shared by
   // every key and need no radix pass.
@@ -324,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     const int dshift = shift - dbits;
     const uint32_t dmask = (1u << dbits) - 1u;
     if (pass >= 2) {  // hist[b] was last read (cluster-wide) two passes ago
-      for (int i = tid; i < kBins; i += kThreads) hist[b][i] = 0;
+      for (int i = tid; i < kBins; i += T) hist[b][i] = 0;
       __syncthreads();
     }
 #pragma unroll
@@ -338,10 +343,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     // Thread t owns per_thread bins just below the per_thread*t highest
     // (descending order); with fewer bins than threads, one bin each.
     const int nb = 1 << dbits;
-    const int per_thread = nb >= kThreads ? nb / kThreads : 1;  // 4, 2 or 1
+    const int per_thread = nb >= T ? nb / T : 1;  // <= kPer
     const bool owns = per_thread * tid < nb;
     const int top = nb - 1 - per_thread * tid;
-    int h[4] = {0, 0, 0, 0};
+    int h[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) h[j] = 0;
     if (owns) {
       if (C > 1) {
 #pragma unroll
@@ -349,20 +356,22 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
           if (r < C) {
             const int* rh = cluster.map_shared_rank(&hist[b][0], r);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < kPer; ++j)
               if (j < per_thread) h[j] += rh[top - j];
           }
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < kPer; ++j)
           if (j < per_thread) h[j] = hist[b][top - j];
       }
     }
-    int total;
-    int above = block_exclusive_sum(h[0] + h[1] + h[2] + h[3], warp_tmp, total);
+    int total, mine_sum = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kPer; ++j) mine_sum += h[j];
+    int above = block_exclusive_sum<kWarps>(mine_sum, warp_tmp, total);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
       if (owns && j < per_thread && above < remaining && remaining <= above + h[j]) {
         s_bin = top - j;
         s_remaining = remaining - above;
@@ -396,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     }
     cnt[c] = (fs << 16) | ft;
   }
-  block_scan_multi<kChunks>(cnt, ex, tot, warp_tmp);
+  block_scan_multi<kChunks, kWarps>(cnt, ex, tot, warp_tmp);
   int tot_strict = 0, tot_tie = 0;
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
@@ -430,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
     for (int j = 0; j < 4; ++j) {
       const uint32_t d = key[4 * c + j] >> shift;
       const bool v = valid_at(4 * c + j);
-      const int id = begin + 4 * (c * kThreads + tid) + j;
+      const int id = begin + 4 * (c * T + tid) + j;
       if (v && d > prefix) {
         sel[sb + min(tb, quota)] = id;
         ++sb;
@@ -446,12 +455,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_kernel(const TopkParams p) {
   // Expansion: one rank per thread and iteration, so consecutive threads
   // write consecutive output columns and issue their page lookups together.
   const int mine = tot_strict + quota;
-  for (int i = tid; i < mine; i += kThreads) {
+  for (int i = tid; i < mine; i += T) {
     const int rank = base_rank + i;
     if (p.expand && rank >= m.complete) break;
     write_rank(p, m, out_row, rank, sel[i]);
   }
-  if (crank == 0 && p.expand) finish_row(p, m, out_row, row);
+  if (crank == 0 && p.expand) finish_row<T>(p, m, out_row, row);
   if (C > 1) cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
@@ -461,21 +470,21 @@ int pow2_ceil(int x) {
   return c;
 }
 
-template <int V>
+template <int T, int V>
 cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
   const int smem = std::max(p.topk, 1) * static_cast<int>(sizeof(int));
   if (smem > kMaxSelBytes) return cudaErrorInvalidValue;
-  cudaError_t e0 = set_attr_once(reinterpret_cast<const void*>(topk_kernel<V>),
+  cudaError_t e0 = set_attr_once(reinterpret_cast<const void*>(topk_kernel<T, V>),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSelBytes);
   if (e0 != cudaSuccess) return e0;
   if (C > 8) {
-    cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_kernel<V>),
+    cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_kernel<T, V>),
                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
   }
   return count_launches(launch_kernel(
-      topk_kernel<V>, dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows)),
-      dim3(kThreads), static_cast<size_t>(std::max(p.topk, 1)) * sizeof(int), stream,
+      topk_kernel<T, V>, dim3(static_cast<unsigned>(C) * static_cast<unsigned>(p.rows)),
+      dim3(T), static_cast<size_t>(std::max(p.topk, 1)) * sizeof(int), stream,
       static_cast<unsigned>(C), p));
 }
 
@@ -486,8 +495,19 @@ int topk_max_width() { return kMaxCluster * kThreads * 32; }
 cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_cluster) {
   TopkParams p = p0;
   if (p.rows <= 0) return cudaSuccess;
-  // Smallest (keys per thread, cluster width) whose slices cover the row.
+  // Rows of one CTA at 8 keys per thread: the narrowest CTA that covers them.
   const int w = std::max(p.width, 1);
+  if (w <= 256 * 8) {
+    p.slice_cap = 256 * 8;
+    if (plan_cluster) *plan_cluster = 1;
+    return launch_v<256, 8>(p, 1, stream);
+  }
+  if (w <= 512 * 8) {
+    p.slice_cap = 512 * 8;
+    if (plan_cluster) *plan_cluster = 1;
+    return launch_v<512, 8>(p, 1, stream);
+  }
+  // Smallest (keys per thread, cluster width) whose slices cover the row.
   int V = 8;
   int C = pow2_ceil((w + kThreads * V - 1) / (kThreads * V));
   if (C > kMaxCluster) {
@@ -497,7 +517,7 @@ cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_clu
   if (C > kMaxCluster) return cudaErrorInvalidValue;
   p.slice_cap = kThreads * V;
   if (plan_cluster) *plan_cluster = C;
-  return V == 8 ? launch_v<8>(p, C, stream) : launch_v<32>(p, C, stream);
+  return V == 8 ? launch_v<kThreads, 8>(p, C, stream) : launch_v<kThreads, 32>(p, C, stream);
 }
 
 }  // namespace qsa
