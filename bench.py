@@ -401,15 +401,20 @@ def main() -> None:
     h2d = dev_meta.numel() + dev_qg.numel()
     d2h = host_out.numel() * host_out.element_size()
     side = torch.cuda.Stream(dev)
+    meta_ready = torch.cuda.Event()
     qg_ready = torch.cuda.Event()
 
     def e2e_step():
         main = torch.cuda.current_stream(dev)
-        side.wait_stream(main)
+        dev_meta.copy_(host_meta, non_blocking=True)
+        # one host->device copy at a time: the indexer's inputs first, then q
+        # and gate (after the previous step's attention, which meta_ready also
+        # orders), overlapped with the indexer and top-k
+        meta_ready.record(main)
+        side.wait_event(meta_ready)
         with torch.cuda.stream(side):
             dev_qg.copy_(host_qg, non_blocking=True)
             qg_ready.record(side)
-        dev_meta.copy_(host_meta, non_blocking=True)
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
             w.token_topk, w.ratio, idx_buf, **w.select_kwargs(),
