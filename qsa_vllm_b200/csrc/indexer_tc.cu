@@ -65,15 +65,22 @@ struct TcCfg {
   static constexpr int kSubBytes = kTileKeys * 128;    // one MMA tile, one sub-row: 16 KB
   static constexpr int kStageBytes = MT * kSub * kSubBytes;  // 32 KB
   static constexpr int kQSubBytes = NQ * 128;
-  // stages in flight: the 32 KB stages that fit beside the two query slots in
-  // half of an SM's shared memory, so two CTAs share an SM (two independent
-  // pipelines per SM, half-size work ranges); at least two stages
-  static constexpr int kSmemBudget = 110 * 1024;
-  static constexpr int kFit = (kSmemBudget - 2 * kSub * kQSubBytes) / (MT * kSub * kTileKeys * 128);
-  static constexpr int S = kFit > 8 ? 8 : (kFit < 2 ? 2 : kFit);
   static constexpr int kAccCols = MT * NQ;             // TMEM columns of one stage's scores
   static constexpr int A = kAccCols <= 64 ? 4 : 2;     // accumulator ring (even: one group each)
   static constexpr int kCols = A * kAccCols < 32 ? 32 : A * kAccCols;
+  // stages in flight: the 32 KB stages that fit beside the two query slots in
+  // half of an SM's shared memory when two CTAs share an SM (two independent
+  // pipelines per SM, half-size work ranges), or in all of it when the CTA's
+  // TMEM columns (more than half of the SM's 512) leave it alone on the SM;
+  // at least two stages
+  static constexpr int kSmemBudget = kCols > 256 ? 220 * 1024 : 110 * 1024;
+  // wide epilogue (rounds of 64 columns): a 16-row x 32-key fp32 tile per
+  // epilogue warp to turn a round's row sums into row-contiguous 16-byte stores
+  static constexpr int kTrFloats = kAccCols > 64 ? 16 * 32 : 1;
+  static constexpr int kTrBytes = kAccCols > 64 ? 4 * kEpiGroups * kTrFloats * 4 : 0;
+  static constexpr int kFit =
+      (kSmemBudget - 2 * kSub * kQSubBytes - kTrBytes) / (MT * kSub * kTileKeys * 128);
+  static constexpr int S = kFit > 8 ? 8 : (kFit < 2 ? 2 : kFit);
   static_assert(S >= 2, "stage ring too small");
 };
 
@@ -83,6 +90,7 @@ struct TcSmem {
   // stage layout: [mma tile m][sub][key row][128 B], each 128-key sub-tile 128B-swizzled
   alignas(1024) uint8_t k[C::S][C::kStageBytes];
   alignas(1024) uint8_t q[2][C::kSub][C::kQSubBytes];  // [slot][sub][column][128 B], swizzled
+  float tr[4 * kEpiGroups][C::kTrFloats];  // per epilogue warp (wide epilogue only)
   SegMeta meta[2];
   float w[2][NQ];
   int limit[2][NQ];  // per row of the segment: columns below this are stored
@@ -254,6 +262,16 @@ __device__ __forceinline__ void score_columns_h(const uint32_t* v, const float* 
                                                 float& carry, int rows_here, const int* lim,
                                                 float* out, int64_t row_stride, int key,
                                                 float scale) {
+  // The rows' store limits are read before the first store: the compiler
+  // cannot move a (generic-pointer) limit load above an earlier logits store,
+  // so loads interleaved with the stores would serialise on their latency.
+  constexpr int kRows = H <= N ? N / H : 1;
+  int lm[kRows];
+#pragma unroll
+  for (int j = 0; j < kRows; ++j) {
+    const int ri = H <= N ? c0 / H + j : c0 / H;
+    lm[j] = ri < rows_here ? lim[ri] : 0;
+  }
   float r[N];
 #pragma unroll
   for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
@@ -267,15 +285,13 @@ __device__ __forceinline__ void score_columns_h(const uint32_t* v, const float* 
 #pragma unroll
     for (int j = 0; j < N / H; ++j) {
       const int ri = c0 / H + j;
-      if (ri < rows_here && key < lim[ri])
-        out[static_cast<int64_t>(ri) * row_stride + key] = r[j * H] * scale;
+      if (key < lm[j]) out[static_cast<int64_t>(ri) * row_stride + key] = r[j * H] * scale;
     }
   } else {
     carry += r[0];
     if ((c0 + N) % H == 0) {
       const int ri = c0 / H;
-      if (ri < rows_here && key < lim[ri])
-        out[static_cast<int64_t>(ri) * row_stride + key] = carry * scale;
+      if (key < lm[0]) out[static_cast<int64_t>(ri) * row_stride + key] = carry * scale;
       carry = 0.f;
     }
   }
@@ -296,6 +312,73 @@ __device__ __forceinline__ void score_columns_pow2(const uint32_t* v, const floa
     case 5: score_columns_h<N, 32>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
     case 6: score_columns_h<N, 64>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
     default: score_columns_h<N, 128>(v, wv, c0, carry, rows_here, lim, out, row_stride, key, scale); break;
+  }
+}
+
+// Wide-epilogue arithmetic for a power-of-two head count 4 <= H <= 32: the
+// R = N/H row sums of each key go through the warp's shared tile (row r, key
+// lane) and leave as 16-byte stores of 4 consecutive keys of one row; a chunk
+// that straddles its row's store limit is written element by element.  The
+// rows' limits are read before the first store (see score_columns_h).
+// Requires 16-byte aligned logits rows.
+template <int N, int H>
+__device__ __forceinline__ void score_columns_tr(const uint32_t* v, const float* wv, int c0,
+                                                 int rows_here, const int* lim, float* out,
+                                                 int64_t row_stride, int key_base, float scale,
+                                                 float* tile) {
+  constexpr int R = N / H;                      // rows of this chunk
+  constexpr int kChunks = R * 8;                // 16-byte chunks: 8 per row of 32 keys
+  constexpr int kPer = (kChunks + 31) / 32;     // chunks per lane
+  const int lane = threadIdx.x & 31;
+  const int row0 = c0 / H;
+  int lm[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int ri = row0 + (lane + 32 * i) / 8;
+    lm[i] = (lane + 32 * i < kChunks && ri < rows_here) ? lim[ri] : 0;
+  }
+  float r[N];
+#pragma unroll
+  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+#pragma unroll
+  for (int step = 1; step < H; step <<= 1) {
+#pragma unroll
+    for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+  }
+#pragma unroll
+  for (int j = 0; j < R; ++j) tile[j * 32 + lane] = r[j * H] * scale;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int q = lane + 32 * i;
+    if (q < kChunks) {
+      const int row = q / 8, k4 = (q % 8) * 4;
+      const float4 val = *reinterpret_cast<const float4*>(tile + row * 32 + k4);
+      const int key = key_base + k4;
+      float* dst = out + static_cast<int64_t>(row0 + row) * row_stride + key;
+      if (key + 3 < lm[i]) {
+        *reinterpret_cast<float4*>(dst) = val;
+      } else {
+        if (key < lm[i]) dst[0] = val.x;
+        if (key + 1 < lm[i]) dst[1] = val.y;
+        if (key + 2 < lm[i]) dst[2] = val.z;
+      }
+    }
+  }
+  __syncwarp();  // the tile is rewritten by the next round
+}
+
+// H = 1 << hshift with 2 <= hshift <= 5 (warp-uniform dispatch).
+template <int N>
+__device__ __forceinline__ void score_columns_tr_pow2(const uint32_t* v, const float* wv, int c0,
+                                                      int hshift, int rows_here, const int* lim,
+                                                      float* out, int64_t row_stride,
+                                                      int key_base, float scale, float* tile) {
+  switch (hshift) {
+    case 2: score_columns_tr<N, 4>(v, wv, c0, rows_here, lim, out, row_stride, key_base, scale, tile); break;
+    case 3: score_columns_tr<N, 8>(v, wv, c0, rows_here, lim, out, row_stride, key_base, scale, tile); break;
+    case 4: score_columns_tr<N, 16>(v, wv, c0, rows_here, lim, out, row_stride, key_base, scale, tile); break;
+    default: score_columns_tr<N, 32>(v, wv, c0, rows_here, lim, out, row_stride, key_base, scale, tile); break;
   }
 }
 
@@ -543,6 +626,11 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const float scale = p.scale;
     const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;  // log2(H), or -1
+    // wide epilogue through the shared tile: 4 <= H <= 32, 16-byte aligned rows
+    const bool tr_path = C::kAccCols > 64 && hshift >= 2 && hshift <= 5 &&
+                         (p.logits_row_stride & 3) == 0 &&
+                         (reinterpret_cast<uintptr_t>(p.logits) & 15) == 0;
+    float* tile = sm.tr[warp - 2];
     int it = 0, j = 0;
     bool ok = true;
     while (ok) {
@@ -619,7 +707,10 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
 #pragma unroll
               for (int c = 0; c < CH; c += 16) tmem_ld16(acc_base + mt * NQ + c0 + c, v + c);
               tmem_wait_ld();
-              if (hshift >= 0)
+              if (tr_path)
+                score_columns_tr_pow2<CH>(v, wv, c0, hshift, rows_here, lim, out,
+                                          p.logits_row_stride, key - lane, scale, tile);
+              else if (hshift >= 0)
                 score_columns_pow2<CH>(v, wv, c0, hshift, acc, rows_here, lim, out,
                                        p.logits_row_stride, key, scale);
               else
