@@ -560,8 +560,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
 constexpr int kMergeHeads = 8;
 template <int D>
 __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParams p) {
-  pdl_wait();
-  pdl_trigger();
   constexpr int DPL = D / 32;  // dims per lane
   const int row = blockIdx.x;
   const int head = blockIdx.y * kMergeHeads + (threadIdx.x >> 5);
@@ -585,6 +583,10 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
   for (int i = 0; i < DPL; ++i)
     gv[i] = gp != nullptr ? __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride])
                           : 0.f;
+  // The gate is a step input that the attention kernel does not write: it is
+  // read above, before waiting on that kernel; its partials are read below.
+  pdl_wait();
+  pdl_trigger();
   float den = 0.f;
   float acc[DPL];
 #pragma unroll

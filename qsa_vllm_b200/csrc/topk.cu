@@ -229,8 +229,6 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
   __shared__ int s_bin, s_remaining, s_bin_count;
   __shared__ int s_counts[2];  // (strictly above, tied) in this CTA's slice
 
-  pdl_wait();
-  pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int crank = static_cast<int>(cluster.block_rank());
@@ -238,6 +236,10 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
   const int tid = threadIdx.x;
   const int topk = p.topk;
   int32_t* out_row = p.output + static_cast<int64_t>(row) * p.out_row_stride;
+  // The row's metadata (request, sequence length, position, visible count,
+  // block table) is step metadata that the preceding kernel (the indexer)
+  // does not write: it is read before waiting on that kernel, so these
+  // dependent loads overlap its tail.  The scores are read after the wait.
   RowMeta m{};
   if (p.expand) m = row_meta(p, row);
   const int length =
@@ -246,6 +248,8 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
                                                 p.token_to_req, p.ratio, row),
               0),
           p.width);
+  pdl_wait();
+  pdl_trigger();
 
   if (length <= topk) {
     // Every column is selected (topk.cu:187-191); no score is read.
