@@ -195,6 +195,8 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   for (int i = 0; i < kLookahead; ++i) prefetch(i % kRing);
 
   int it = 0, k = 0, own = 0;
+  static_assert(kStages <= 32, "one bit per stage");
+  uint32_t zeroed = 0;  // bit s: this producer's last fill of stage s wrote zeros
   bool ok = true;
   for (; k < units && ok; ++k) {
     const Unit x = unit_of<TT>(p, groups, ua, ub, k);
@@ -246,9 +248,10 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       // mapping as the prefetch), complete once all but the newest
       // kLookahead-1 groups are.
       cp_async_wait<kLookahead - 1>();
-      // generic-proxy zero fills of an earlier use of this stage are ordered
-      // before the async-proxy (bulk copy) writes issued below
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      // generic-proxy zero fills of this producer's earlier use of this stage
+      // are ordered before the async-proxy (bulk copy) writes issued below;
+      // without such fills there is nothing to order
+      if ((zeroed >> s) & 1u) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       uint8_t* stage = sm.stage[s];
       const int slot = own % kRing;
       int64_t off_k[2], off_v[2];
@@ -285,6 +288,9 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
           for (int c = 0; c < kRow / 16; ++c) z[c] = make_uint4(0, 0, 0, 0);
         }
       }
+      const bool filled = __any_sync(0xffffffffu, (!valid[0] && lane < TT) ||
+                                                      (!valid[1] && lane + 32 < TT));
+      zeroed = filled ? zeroed | (1u << s) : zeroed & ~(1u << s);
       const unsigned lo = __ballot_sync(0xffffffffu, valid[0]);
       const unsigned hi = __ballot_sync(0xffffffffu, valid[1]);
       // A 4-token block whose slots are consecutive in a slot-contiguous cache
