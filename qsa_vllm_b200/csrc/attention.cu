@@ -14,10 +14,12 @@
 //    few CTAs, each writing one partial of it.  A pair covers HB = up to 4
 //    KV heads of one row: a selected token's K||V
 //    rows of those heads are one contiguous run (2 KB at head_dim 128), moved
-//    by ONE bulk copy (cp.async.bulk on the TMA engine) into a 4-stage
+//    by ONE bulk copy (cp.async.bulk on the TMA engine) into a 6-stage
 //    shared-memory ring guarded by mbarriers.  Token rows are padded by 16 B
 //    so ldmatrix reads are bank-conflict free.  Invalid tokens are zero-filled.
-//  * One producer warp issues the copies.  The token ids it needs are
+//  * Three producer warps issue the copies, each for every third tile (two
+//    stages each: the copy issue itself bounds L2-resident gathers).  The
+//    token ids a producer needs are
 //    streamed into a small shared-memory ring by cp.async several tiles
 //    ahead, and the unit's query rows are bulk-copied into a double buffer,
 //    so no global-load latency sits on the issue path.
@@ -48,9 +50,14 @@ constexpr int kConsumerWarps = kGroups * kGroupWarps;
 // not a multiple of kGroups, consecutive uses of a stage would alternate groups
 // and a group running two barrier phases ahead would alias the parity wait.
 static_assert(kStages % kGroups == 0, "each stage must belong to one consumer group");
-static_assert(kStages % kGroups == 0 && kGroups == 2, "producer p feeds consumer group p");
-constexpr int kThreads = (kConsumerWarps + kGroups) * 32;
-constexpr int kProducers = kGroups;  // producer warp p fills stages it % kProducers == p
+// Producer warp p fills the tiles it % kProducers == p: issuing a tile's bulk
+// copies costs a warp ~0.6 us, which bounds L2-resident (prefill) gathers, so
+// three warps share the issue.  Stage s is always filled by producer
+// s % kProducers, which takes its stages in order: its empty-barrier waits
+// are never more than one phase ahead (no parity aliasing).
+constexpr int kProducers = 3;
+static_assert(kStages % kProducers == 0, "each stage must belong to one producer");
+constexpr int kThreads = (kConsumerWarps + kProducers) * 32;
 constexpr int kRing = 8;       // token-id ring slots per producer (one per own tile)
 constexpr int kLookahead = 4;  // own tiles of token ids in flight ahead of the copies
 static_assert(kLookahead < kRing, "ring / lookahead sizes");
@@ -67,7 +74,7 @@ struct Smem {
   static __device__ __forceinline__ int tok_off(int j) { return (j >> 2) * kBlk + (j & 3) * kRow; }
   alignas(128) uint8_t stage[kStages][(kTT / 4) * kBlk];
   alignas(128) uint8_t q[2][kQRows * 2 * D];
-  int32_t ring[kGroups][kRing][64];
+  int32_t ring[kProducers][kRing][64];
   uint64_t mask[kStages];
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -195,8 +202,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   for (int i = 0; i < kLookahead; ++i) prefetch(i % kRing);
 
   int it = 0, k = 0, own = 0;
-  static_assert(kStages <= 32, "one bit per stage");
-  uint32_t zeroed = 0;  // bit s: this producer's last fill of stage s wrote zeros
+
   bool ok = true;
   for (; k < units && ok; ++k) {
     const Unit x = unit_of<TT>(p, groups, ua, ub, k);
@@ -232,7 +238,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         p.block_table + static_cast<int64_t>(req_ok ? req : 0) * p.table_row_stride;
     const int64_t head0 = static_cast<int64_t>(x.hg) * HB;
     for (int t = x.t0; t < x.t1; ++t, ++it) {
-      if (it % kProducers != pw) continue;  // the other producer's tile
+      if (it % kProducers != pw) continue;  // another producer's tile
       const int s = it % kStages;
       if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1)) {
         record_error(p.err, kDeviceErrWaitTimeout);
@@ -248,10 +254,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       // mapping as the prefetch), complete once all but the newest
       // kLookahead-1 groups are.
       cp_async_wait<kLookahead - 1>();
-      // generic-proxy zero fills of this producer's earlier use of this stage
-      // are ordered before the async-proxy (bulk copy) writes issued below;
-      // without such fills there is nothing to order
-      if ((zeroed >> s) & 1u) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
       uint8_t* stage = sm.stage[s];
       const int slot = own % kRing;
       int64_t off_k[2], off_v[2];
@@ -288,9 +291,11 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
           for (int c = 0; c < kRow / 16; ++c) z[c] = make_uint4(0, 0, 0, 0);
         }
       }
-      const bool filled = __any_sync(0xffffffffu, (!valid[0] && lane < TT) ||
-                                                      (!valid[1] && lane + 32 < TT));
-      zeroed = filled ? zeroed | (1u << s) : zeroed & ~(1u << s);
+      // Zero fills (generic proxy) are ordered before this stage's next bulk
+      // copies (async proxy), issued after the full -> empty barrier chain;
+      // without fills there is nothing to order.
+      if (__any_sync(0xffffffffu, (!valid[0] && lane < TT) || (!valid[1] && lane + 32 < TT)))
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       const unsigned lo = __ballot_sync(0xffffffffu, valid[0]);
       const unsigned hi = __ballot_sync(0xffffffffu, valid[1]);
       // A 4-token block whose slots are consecutive in a slot-contiguous cache
