@@ -583,7 +583,6 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
   const int hg = (head / (p.q_heads / p.kv_heads)) / p.heads_per_unit;
   const int64_t first = (static_cast<int64_t>(row) * groups + hg) * p.pair_tiles;
   const int P = (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) * p.slot_group;
-  const int lane = threadIdx.x & 31;
   // the gate does not depend on the partials: its loads go out first
   float gv[DPL];
   const __nv_bfloat16* gp = p.gate == nullptr ? nullptr
