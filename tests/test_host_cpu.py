@@ -339,3 +339,35 @@ def test_select_paged_tokens_chunking_with_oracle_kernels(monkeypatch, given_vis
                                                       vis[r:r + 1], 80), nan=0.0)[0]
     ref, _ = O.topk_expand(logits, vis, pos, seq, t2r, None, topk + ratio - 1, ratio)
     assert np.array_equal(out.numpy(), ref)
+
+
+# ------------------------------------------------------- synthetic workloads
+def test_select_kwargs_decode_mtp_and_prefill():
+    from qsa_vllm_b200.synthetic import make_workload
+    w = make_workload("cfg2_32k_mtp2", device="cpu", batch=3, seq_len=1024)
+    k = w.select_kwargs()
+    assert w.rows == 6 and k["num_decodes"] == 3 and k["num_decode_tokens"] == 6
+    assert k["decode_query_len"] == 2 and k["max_query_len"] == 2
+    assert w.positions.tolist() == [1022, 1023] * 3
+    p = make_workload("cfg1", device="cpu", batch=2, seq_len=512, new_tokens=64)
+    kp = p.select_kwargs()
+    assert "num_decodes" not in kp and kp["max_query_len"] == 64
+
+
+def test_prepare_inputs_metadata_follow_the_workload():
+    from qsa_vllm_b200.synthetic import make_prepare_inputs, make_workload
+    w = make_workload("cfg2", device="cpu", seed=8, batch=8)
+    a = make_prepare_inputs(w, state_size=64)
+    pos = w.positions
+    r, page = w.ratio, w.page_size
+    comp = a["compressed_metadata"].slot_mapping
+    # compressed slots exactly at compression boundaries
+    assert torch.equal(comp >= 0, (pos + 1) % r == 0)
+    # main slots: the token's page in its request's block table
+    req = w.token_to_req.long()
+    expect = w.block_table.long()[req, pos // page] * page + pos % page
+    assert torch.equal(a["main_slots"], expect)
+    # one work item per request for decode rows (max(groups, 1))
+    kw = a["compressed_metadata"].k_work_metadata
+    assert kw.shape == (8, 2) and kw[:, 1].eq(0).all()
+    assert torch.equal(a["raw_metadata"].slot_mapping, req * 64 + pos % 64)
