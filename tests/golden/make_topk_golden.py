@@ -9,8 +9,8 @@ for sm_100a, op namespace renamed to ``yulan_qsa_ref_kernels``):
 For every case of ``tests/topk_cases.standard_cases()`` it calls
 ``torch.ops.yulan_qsa_ref_kernels.topk_expand`` exactly as the reference
 wrapper does (ops/topk.py:29-39: dummy tensors for unused table / counts) and
-stores inputs and outputs.  Output defaults to ``gpurun_out/reference_topk.npz``;
-the committed copy lives at ``tests/golden/reference_topk.npz``.
+stores inputs and outputs.  Output defaults to ``reference_topk.npz`` in the
+current directory; the committed copy lives at ``tests/golden/reference_topk.npz``.
 """
 
 from __future__ import annotations
@@ -50,7 +50,7 @@ def main(out_path: str | None = None) -> None:
                                         int(c["store_counts"])])
         out[f"{name}__output"] = output.cpu().numpy()
         out[f"{name}__counts"] = counts.cpu().numpy()
-    path = Path(out_path) if out_path else ROOT / "gpurun_out" / "reference_topk.npz"
+    path = Path(out_path) if out_path else Path("reference_topk.npz")
     path.parent.mkdir(parents=True, exist_ok=True)
     np.savez_compressed(path, **out)
     print("wrote", path, len(out), "arrays")
