@@ -493,6 +493,18 @@ def test_decode_step_mtp2(dev):
     _check_decode_rows(w, dev, out_idx, counts, out, [0, 1, 14, 15])
 
 
+@pytest.mark.parametrize("tp,rank", [(4, 3), (8, 5)])
+def test_decode_step_head_shard(dev, tp, rank):
+    """One rank's share under head sharding (the multi-GPU benchmark's layout):
+    tp 4 keeps 8 query heads / 1 KV head, tp 8 keeps 4 query heads of a KV
+    head replicated on two ranks; the indexer and top-k are replicated."""
+    from qsa_vllm_b200.synthetic import make_workload
+    w = make_workload("cfg2_32k", device=dev, seed=9, batch=8).shard_heads(tp, rank)
+    assert w.q.shape[1] == 32 // tp and w.kv.shape[2] == 1
+    out_idx, counts, out = _decode_step(w, dev)
+    _check_decode_rows(w, dev, out_idx, counts, out, [0, 3, 7])
+
+
 def test_prefill_step_cfg1(dev):
     """Chunked prefill: logical ids, per-row causal visibility, many rows."""
     from qsa_vllm_b200.indexer import indexer_scores, select_paged_tokens
