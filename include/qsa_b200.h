@@ -274,12 +274,19 @@ QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_
  * No counterpart in the reference.  Same arguments and results as
  * qsa_sparse_attention without (workspace, workspace_bytes): the split-K
  * scratch is a file-scope device array of QSA_STATIC_SCRATCH_BYTES per device,
- * whose address is resolved once per device; nothing is allocated.
- *   - Calls needing more scratch than QSA_STATIC_SCRATCH_BYTES (see
- *     qsa_sparse_attention_workspace_bytes; 8 MiB for 64 decode rows of
+ * whose address is looked up (cudaGetSymbolAddress, no allocation) on each
+ * call with the caller's device current; nothing is allocated.
+ *   - The array exists in every context that loads this library's module
+ *     (at the first call under lazy module loading, at library load under
+ *     CUDA_MODULE_LOADING=EAGER) and is held until the context ends.  Make the
+ *     first call on a device before any stream capture, so the module load
+ *     does not happen inside a capture.
+ *   - Shapes are validated first (QSA_ERR_INVALID / QSA_ERR_UNSUPPORTED);
+ *     well-formed calls needing more scratch than QSA_STATIC_SCRATCH_BYTES
+ *     (see qsa_sparse_attention_workspace_bytes; 8 MiB for 64 decode rows of
  *     32 query / 4 KV heads x 128 at top-k 2048) return QSA_ERR_WORKSPACE.
  *   - Nothing in the scratch has to start at zero: each call writes every
- *     partial slot it reads.
+ *     partial slot it reads (as an empty partial when a bounded wait gave up).
  *   - One scratch array serves all calls on a device: calls whose kernels
  *     overlap on the GPU (other streams or host threads) race on it; the
  *     caller must serialise them.

@@ -9,14 +9,18 @@ the command line (``-Dyulan_qsa_kernels=yulan_qsa_ref_kernels``) so the
 reference registers ``torch.ops.yulan_qsa_ref_kernels.topk_expand`` and can be
 loaded beside this package's own ``torch.ops.yulan_qsa_kernels``.
 
-    python oracle/build_ref.py [/path/to/reference]
+    python oracle/build_ref.py [REFERENCE_ROOT]
 
-Nothing here runs unless the reference tree is present (development
-container only); the GPU box uses the prebuilt library.
+REFERENCE_ROOT is the reference checkout (the directory holding
+``yulan_qsa_vllm/``): the argument, else ``$QSA_REFERENCE_ROOT``, else a
+checkout named ``reference`` beside this repository.  Nothing here runs unless
+that tree is present (development container only); the GPU box uses the
+prebuilt library.
 """
 
 from __future__ import annotations
 
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -25,8 +29,19 @@ HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "libqsa_ref_topk.so"
 
 
-def build(ref_root: str = "/root/reference", force: bool = False) -> Path | None:
-    src = Path(ref_root) / "yulan_qsa_vllm" / "ops" / "csrc" / "topk.cu"
+def reference_root(explicit: str | None = None) -> Path:
+    """The reference checkout: ``explicit``, else ``$QSA_REFERENCE_ROOT``, else
+    the directory ``reference`` next to this repository's root."""
+    if explicit:
+        return Path(explicit)
+    env = os.environ.get("QSA_REFERENCE_ROOT")
+    if env:
+        return Path(env)
+    return HERE.parent.parent / "reference"
+
+
+def build(ref_root: str | None = None, force: bool = False) -> Path | None:
+    src = reference_root(ref_root) / "yulan_qsa_vllm" / "ops" / "csrc" / "topk.cu"
     if not src.exists():
         return OUT if OUT.exists() else None
     if OUT.exists() and not force and OUT.stat().st_mtime > src.stat().st_mtime:

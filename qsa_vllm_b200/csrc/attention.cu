@@ -507,7 +507,19 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     // tokens of the unit, written straight from registers (base-2 LSE, the
     // reference's split-K format).  The merge kernel combines the partials of
     // all (split, group, sub-tile) slots of a head.
-    if (aborted) continue;  // results of an aborted launch are not written
+    // An aborted launch still writes this warp's slots, as empty partials
+    // (O = 0, LSE = -inf): the merge gives them no weight and never combines
+    // values that another call left in the workspace.
+    aborted = __any_sync(0xffffffffu, aborted);
+    if (aborted) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+          o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
+      }
+    }
     const int pslot = (x.split * kGroups + cg) * SUB + sub;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {

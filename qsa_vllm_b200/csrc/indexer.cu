@@ -255,18 +255,13 @@ cudaError_t launch_d(const IndexerParams& p, int nt, dim3 grid, int rpc, int kpc
   return cudaErrorInvalidValue;
 }
 
-// QSA_INDEXER_MMA_SYNC=1 selects the mma.sync kernel for every shape (both
-// formulations compute the same scores; tests run the two against the oracle).
-bool indexer_force_mma() {
-  const char* v = std::getenv("QSA_INDEXER_MMA_SYNC");
-  return v != nullptr && v[0] == '1';
-}
-
 }  // namespace
 
 cudaError_t launch_indexer(const IndexerParams& p, cudaStream_t stream) {
   if (p.num_rows <= 0) return cudaSuccess;
-  if (indexer_tc_eligible(p) && !indexer_force_mma()) {
+  // The tensor-core kernel takes every shape its tensor maps can address;
+  // the mma.sync kernel covers the rest (pages not a multiple of 8 rows).
+  if (indexer_tc_eligible(p)) {
     const cudaError_t e = launch_indexer_tc(p, stream);
     if (e != cudaErrorNotSupported) return e;  // else: tensor maps refused these strides
   }

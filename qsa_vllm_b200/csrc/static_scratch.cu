@@ -4,13 +4,14 @@
 // instead of a caller-provided buffer; nothing here allocates.
 //
 // Nothing in the scratch must start at zero: every partial slot the merge
-// reads is written by the main kernel of the same call, so no clearing pass is
-// needed.  There is one scratch array per device, shared by every call on that
-// device: calls whose kernels overlap on the GPU (other streams, other host
-// threads) race on it and must be serialised by the caller.
+// reads is written by the main kernel of the same call (as an empty partial
+// when a bounded wait gave up), so no clearing pass is needed.  There is one
+// scratch array per device, shared by every call on that device: calls whose
+// kernels overlap on the GPU (other streams, other host threads) race on it
+// and must be serialised by the caller.
 #include <cuda_runtime.h>
 
-#include <mutex>
+#include <cstring>
 
 #include "../../include/qsa_b200.h"
 #include "kernels.h"
@@ -20,25 +21,18 @@ namespace {
 constexpr size_t kScratchBytes = QSA_STATIC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
 
-constexpr int kMaxScratchDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxScratchDevices] = {};
-
-// Device address of this device's scratch: resolved once per device, with
-// that device current.
+// Device address of the current device's scratch.  Looked up on every call
+// (the lookup allocates nothing), so it stays right if the context of a
+// device is torn down and recreated.  On failure the pending CUDA error is
+// cleared, so it does not surface in an unrelated later call.
 cudaError_t scratch_address(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
-    if (e != cudaSuccess) return e;
-    g_scratch_addr[dev] = ptr;
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
   }
-  *out = g_scratch_addr[dev];
+  *out = ptr;
   return cudaSuccess;
 }
 
@@ -57,28 +51,30 @@ extern "C" int qsa_sparse_attention_static_scratch(
     int64_t out_head_stride, int32_t indices_are_physical, int32_t use_decode_kernel,
     void* stream) {
   const char* who = "qsa_sparse_attention_static_scratch";
-  if (rows > 0 && num_q_heads > 0 && num_kv_heads > 0 && head_dim > 0 && topk_width >= 0) {
-    const size_t need = qsa_sparse_attention_workspace_bytes(
-        rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel);
-    if (need > kScratchBytes)
-      return qsa::set_last_error(
-          QSA_ERR_WORKSPACE,
-          "%s: this call needs %zu bytes of split-K scratch, above the static maximum of %zu "
-          "bytes (QSA_STATIC_SCRATCH_BYTES); use qsa_sparse_attention with a caller workspace",
-          who, need, kScratchBytes);
-  }
   void* scratch = nullptr;
   const cudaError_t e = scratch_address(&scratch);
   if (e != cudaSuccess)
     return qsa::set_last_error(QSA_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who,
                                cudaGetErrorString(e));
-  return qsa_sparse_attention(q, q_row_stride, q_head_stride, rows, num_q_heads, head_dim,
-                              k_cache, k_block_stride, k_token_stride, k_head_stride, v_cache,
-                              v_block_stride, v_token_stride, v_head_stride, num_blocks,
-                              page_size, num_kv_heads, indices, indices_row_stride, topk_width,
-                              block_table, table_row_stride, table_width, num_requests,
-                              token_to_req, valid_counts, gate, gate_row_stride,
-                              gate_head_stride, gate_dim_stride, out, out_row_stride,
-                              out_head_stride, indices_are_physical, use_decode_kernel, scratch,
-                              kScratchBytes, stream);
+  // The caller-workspace entry point validates the shapes first and only then
+  // compares the plan's scratch need with the size it is given, so malformed
+  // calls get QSA_ERR_INVALID / QSA_ERR_UNSUPPORTED, and well-formed calls
+  // above the static maximum get QSA_ERR_WORKSPACE (reworded below).
+  const int status = qsa_sparse_attention(
+      q, q_row_stride, q_head_stride, rows, num_q_heads, head_dim, k_cache, k_block_stride,
+      k_token_stride, k_head_stride, v_cache, v_block_stride, v_token_stride, v_head_stride,
+      num_blocks, page_size, num_kv_heads, indices, indices_row_stride, topk_width, block_table,
+      table_row_stride, table_width, num_requests, token_to_req, valid_counts, gate,
+      gate_row_stride, gate_head_stride, gate_dim_stride, out, out_row_stride, out_head_stride,
+      indices_are_physical, use_decode_kernel, scratch, kScratchBytes, stream);
+  if (status == QSA_ERR_WORKSPACE) {
+    const size_t need = qsa_sparse_attention_workspace_bytes(
+        rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel);
+    return qsa::set_last_error(
+        QSA_ERR_WORKSPACE,
+        "%s: this call needs %zu bytes of split-K scratch, above the static maximum of %zu "
+        "bytes (QSA_STATIC_SCRATCH_BYTES); use qsa_sparse_attention with a caller workspace",
+        who, need, kScratchBytes);
+  }
+  return status;
 }

@@ -2,7 +2,7 @@
 
 Run in the development container, where the reference package is readable:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py REFERENCE_ROOT   (or set QSA_REFERENCE_ROOT)
 
 It copies the reference package ``yulan_qsa_vllm`` to a temporary directory
 (importing it in place would JIT-compile ``ops/csrc/topk.cu`` into the source
@@ -43,6 +43,16 @@ import torch  # noqa: E402
 HERE = Path(__file__).resolve().parent
 
 
+
+def _reference_root(explicit: str | None) -> Path:
+    """The reference checkout (holding ``yulan_qsa_vllm/``): the command-line
+    argument, else ``$QSA_REFERENCE_ROOT``; one of them is required."""
+    root = explicit or os.environ.get("QSA_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: pass the reference checkout as the first argument "
+                         "or set QSA_REFERENCE_ROOT")
+    return Path(root)
+
 def _import_reference(ref_root: Path):
     tmp = Path(tempfile.mkdtemp(prefix="qsa_ref_"))
     shutil.copytree(ref_root / "yulan_qsa_vllm", tmp / "yulan_qsa_vllm")
@@ -65,7 +75,8 @@ def bits16(x: torch.Tensor) -> np.ndarray:
     return x.to(torch.bfloat16).view(torch.int16).numpy()
 
 
-def main(ref_root: str = "/root/reference") -> None:
+def main(ref_root: str | None = None) -> None:
+    ref_root = str(_reference_root(ref_root))
     indexer, qsa, tmp = _import_reference(Path(ref_root))
     gen = torch.Generator().manual_seed(1234)
     out: dict[str, np.ndarray] = {}

@@ -154,19 +154,16 @@ def _indexer_case(dev, *, rows_per_req, requests, heads, dim, page, width, seed,
     return q, kc, table, vis, w
 
 
-# page % 8 == 0 runs the tcgen05/TMA kernel, other pages (and mma_sync=True,
-# through QSA_INDEXER_MMA_SYNC=1) the mma.sync kernel
-@pytest.mark.parametrize("heads,dim,page,dql,weights,mma_sync", [
-    (8, 64, 64, 1, True, False), (4, 64, 16, 1, False, False), (4, 128, 16, 2, True, False),
-    (16, 64, 32, 1, True, False), (1, 64, 16, 1, False, False), (2, 128, 8, 4, False, False),
-    (64, 64, 64, 2, True, False), (48, 128, 24, 1, True, False), (8, 64, 128, 1, True, False),
-    (8, 64, 256, 1, True, False), (8, 64, 4, 1, True, False), (4, 128, 12, 2, True, False),
-    (8, 64, 64, 1, True, True), (4, 128, 16, 2, True, True)])
-def test_indexer_decode_matches_oracle(dev, monkeypatch, heads, dim, page, dql, weights,
-                                       mma_sync):
+# page % 8 == 0 runs the tcgen05/TMA kernel; other pages (4, 12, 60, 20) run
+# the mma.sync kernel, the path for pages a TMA box cannot address
+@pytest.mark.parametrize("heads,dim,page,dql,weights", [
+    (8, 64, 64, 1, True), (4, 64, 16, 1, False), (4, 128, 16, 2, True),
+    (16, 64, 32, 1, True), (1, 64, 16, 1, False), (2, 128, 8, 4, False),
+    (64, 64, 64, 2, True), (48, 128, 24, 1, True), (8, 64, 128, 1, True),
+    (8, 64, 256, 1, True), (8, 64, 4, 1, True), (4, 128, 12, 2, True),
+    (8, 64, 60, 1, True), (4, 128, 20, 2, True)])
+def test_indexer_decode_matches_oracle(dev, heads, dim, page, dql, weights):
     from qsa_vllm_b200.indexer import indexer_scores
-    if mma_sync:
-        monkeypatch.setenv("QSA_INDEXER_MMA_SYNC", "1")
     q, kc, table, vis, w = _indexer_case(dev, rows_per_req=dql, requests=5, heads=heads, dim=dim,
                                          page=page, width=40, seed=heads * dim + page,
                                          weights=weights)
@@ -181,13 +178,11 @@ def test_indexer_decode_matches_oracle(dev, monkeypatch, heads, dim, page, dql, 
     torch.testing.assert_close(got[m], ref[m], rtol=SCORE_RTOL, atol=SCORE_ATOL)
 
 
-@pytest.mark.parametrize("heads,dim,page,mma_sync", [
-    (4, 64, 16, False), (8, 64, 16, False), (4, 128, 16, False), (64, 64, 16, False),
-    (48, 128, 16, False), (8, 64, 64, False), (8, 64, 6, False), (8, 64, 16, True)])
-def test_indexer_prefill_matches_oracle(dev, monkeypatch, heads, dim, page, mma_sync):
+@pytest.mark.parametrize("heads,dim,page", [
+    (4, 64, 16), (8, 64, 16), (4, 128, 16), (64, 64, 16),
+    (48, 128, 16), (8, 64, 64), (8, 64, 6), (8, 64, 12)])
+def test_indexer_prefill_matches_oracle(dev, heads, dim, page):
     from qsa_vllm_b200.indexer import indexer_scores
-    if mma_sync:
-        monkeypatch.setenv("QSA_INDEXER_MMA_SYNC", "1")
     g = torch.Generator().manual_seed(heads + dim + page)
     width, requests = 384 // page, 3
     qlens = [70, 1, 45]

@@ -200,7 +200,7 @@ def test_graph_dispatch_patch_with_fake_vllm():
     gd.install_short_decode_dispatch(ModelGraphManager, GraphManager, Runner, FULL, Desc)
     m = ModelGraphManager()
     m._init_candidates()
-    cols = sorted(d.qsa_columns for d in m._capture_descs[FULL])
+    cols = sorted(d.logits_columns for d in m._capture_descs[FULL])
     assert cols == [0, 32768]
     seen = m.capture(lambda desc, warm: (lambda mode: gd.decode_logits_columns(10, 4, 50000)))
     assert sorted(seen) == [32768, 50000]
@@ -208,10 +208,10 @@ def test_graph_dispatch_patch_with_fake_vllm():
     runner.req_states = SimpleNamespace(num_computed_tokens_np=np.array([100, 600000]))
     batch = SimpleNamespace(idx_mapping_np=np.array([0]), num_scheduled_tokens=np.array([1]))
     runner.gather_batch_req_state(batch, False)
-    assert gd.runtime_columns() == 32768 and m.dispatch(8).qsa_columns == 32768
+    assert gd.runtime_columns() == 32768 and m.dispatch(8).logits_columns == 32768
     batch.idx_mapping_np = np.array([1])
     runner.gather_batch_req_state(batch, False)
-    assert gd.runtime_columns() == 0 and m.dispatch(8).qsa_columns == 0
+    assert gd.runtime_columns() == 0 and m.dispatch(8).logits_columns == 0
 
 
 # ----------------------------------------------------------------- sharding

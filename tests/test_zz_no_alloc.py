@@ -90,3 +90,25 @@ def test_static_scratch_rejects_calls_above_its_maximum():
     assert "static maximum" in lib.qsa_last_error().decode()
     assert _lib.kernel_launches() == n0
     assert ctypes.sizeof(ctypes.c_size_t) == 8
+
+
+def test_static_scratch_validates_shapes_before_its_maximum():
+    """A malformed call that would also exceed the static maximum is refused as
+    malformed (invalid / unsupported shape), not as a scratch overflow."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.ensure_device(dev)
+    lib = _lib.load_library()
+    rows, width = 4096, 2051
+    x = torch.zeros(16, dtype=torch.int32, device=dev)
+    n0 = _lib.kernel_launches()
+    for hq, hkv, d, expected in ((32, 4, 256, 2),   # head dim 256: QSA_ERR_UNSUPPORTED
+                                 (30, 4, 128, 1)):  # 30 query heads over 4 KV: QSA_ERR_INVALID
+        status = lib.qsa_sparse_attention_static_scratch(
+            x.data_ptr(), hq * d, d, rows, hq, d,
+            x.data_ptr(), 0, 0, 0, x.data_ptr(), 0, 0, 0, 1, 64, hkv,
+            x.data_ptr(), width, width, x.data_ptr(), 1, 1, 1, x.data_ptr(), x.data_ptr(),
+            None, 0, 0, 0, x.data_ptr(), hq * d, d, 1, 1,
+            torch.cuda.current_stream().cuda_stream)
+        assert status == expected, (hq, hkv, d, status, lib.qsa_last_error().decode())
+    assert _lib.kernel_launches() == n0
