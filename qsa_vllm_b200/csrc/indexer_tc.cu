@@ -41,11 +41,11 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace qsa {
 namespace {
 
-constexpr int kTileKeys = 128;  // keys per tcgen05.mma (M)
 constexpr int kEpiGroups = 2;   // epilogue warpgroups; group g takes stages g, g+2, ...
 constexpr int kTcThreads = (2 + 4 * kEpiGroups) * 32;  // producer, MMA, 8 epilogue warps
 
@@ -99,85 +99,6 @@ struct TcSmem {
   int abort_flag;
 };
 
-// UMMA shared-memory descriptor of a K-major operand in the 128-byte swizzle
-// atom layout: rows of 128 B, 8-row atoms 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
-  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused: swizzled)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: 8-row atoms
-  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;                  // layout: 128-byte swizzle
-  return d;
-}
-
-// Instruction descriptor of kind::f16: D fp32, A and B bf16, both K-major, M x N.
-template <int M, int N>
-constexpr uint32_t instr_desc() {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                            int c2, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, bool accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1 : 0)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// A read-only load that is issued exactly where it is written (the page-id
-// window is fetched ahead of its use).
-__device__ __forceinline__ int ld_once(const int32_t* ptr) {
-  int v;
-  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(ptr));
-  return v;
-}
-
-// Warp-uniform bounded wait: true when the phase completed for every lane.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
-}
-
-__device__ __forceinline__ bool aborted(const int* flag) {
-  return __any_sync(0xffffffffu, *reinterpret_cast<const volatile int*>(flag) != 0);
-}
-
 struct TcGeometry {
   int segments;       // segment slots (prefill: requests x row tiles, some empty)
   int row_tiles;      // prefill row tiles per request (1 for decode)
@@ -204,7 +125,13 @@ __device__ __forceinline__ void segment_rows(const IndexerParams& p, const TcGeo
   r1 = min(r0 + g.rows_per_seg, re);
 }
 
-// Epilogue arithmetic, sequential form (any head count): ReLU, head weight,
+// Epilogue arithmetic.  Every product and sum is rounded on its own
+// (__fmul_rn / __fadd_rn: no FMA contraction), and for a given head count the
+// heads of a row are added in one fixed order (a log-depth tree over adjacent
+// columns for a power-of-two count), so every formulation below, and the
+// fused decode selection (select_decode.cu), give the same fp32 bits.
+//
+// Sequential form (any head count): ReLU, head weight,
 // sum of the H heads of each row, scaled store.  (acc, h, ri) carry a row
 // across calls.
 template <int N>
@@ -214,10 +141,10 @@ __device__ __forceinline__ void score_columns_seq(const uint32_t* v, const float
                                                   int64_t row_stride, int key, float scale) {
   float r[N];
 #pragma unroll
-  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+  for (int x = 0; x < N; ++x) r[x] = __fmul_rn(fmaxf(__uint_as_float(v[x]), 0.f), wv[c0 + x]);
 #pragma unroll
   for (int x = 0; x < N; ++x) {
-    acc += r[x];
+    acc = __fadd_rn(acc, r[x]);
     if (++h == H) {
       if (ri < rows_here && key < lim[ri]) out[static_cast<int64_t>(ri) * row_stride + key] = acc * scale;
       acc = 0.f;
@@ -238,12 +165,12 @@ __device__ __forceinline__ void score_columns_pow2_reg(const uint32_t* v, const 
                                                        float scale) {
   float r[N];
 #pragma unroll
-  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wr[x];
+  for (int x = 0; x < N; ++x) r[x] = __fmul_rn(fmaxf(__uint_as_float(v[x]), 0.f), wr[x]);
 #pragma unroll
   for (int step = 1; step < N; step <<= 1) {
     if (step < H) {
 #pragma unroll
-      for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+      for (int x = 0; x + step < N; x += 2 * step) r[x] = __fadd_rn(r[x], r[x + step]);
     }
   }
 #pragma unroll
@@ -274,12 +201,12 @@ __device__ __forceinline__ void score_columns_h(const uint32_t* v, const float* 
   }
   float r[N];
 #pragma unroll
-  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+  for (int x = 0; x < N; ++x) r[x] = __fmul_rn(fmaxf(__uint_as_float(v[x]), 0.f), wv[c0 + x]);
   constexpr int kSpan = H < N ? H : N;  // columns summed per tree
 #pragma unroll
   for (int step = 1; step < kSpan; step <<= 1) {
 #pragma unroll
-    for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+    for (int x = 0; x + step < N; x += 2 * step) r[x] = __fadd_rn(r[x], r[x + step]);
   }
   if constexpr (H <= N) {
 #pragma unroll
@@ -288,7 +215,7 @@ __device__ __forceinline__ void score_columns_h(const uint32_t* v, const float* 
       if (key < lm[j]) out[static_cast<int64_t>(ri) * row_stride + key] = r[j * H] * scale;
     }
   } else {
-    carry += r[0];
+    carry = __fadd_rn(carry, r[0]);
     if ((c0 + N) % H == 0) {
       const int ri = c0 / H;
       if (key < lm[0]) out[static_cast<int64_t>(ri) * row_stride + key] = carry * scale;
@@ -339,11 +266,11 @@ __device__ __forceinline__ void score_columns_tr(const uint32_t* v, const float*
   }
   float r[N];
 #pragma unroll
-  for (int x = 0; x < N; ++x) r[x] = fmaxf(__uint_as_float(v[x]), 0.f) * wv[c0 + x];
+  for (int x = 0; x < N; ++x) r[x] = __fmul_rn(fmaxf(__uint_as_float(v[x]), 0.f), wv[c0 + x]);
 #pragma unroll
   for (int step = 1; step < H; step <<= 1) {
 #pragma unroll
-    for (int x = 0; x + step < N; x += 2 * step) r[x] += r[x + step];
+    for (int x = 0; x + step < N; x += 2 * step) r[x] = __fadd_rn(r[x], r[x + step]);
   }
 #pragma unroll
   for (int j = 0; j < R; ++j) tile[j * 32 + lane] = r[j * H] * scale;
@@ -748,29 +675,6 @@ __global__ void __launch_bounds__(kTcThreads) indexer_tc_kernel(
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
-                                         cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-int gcd_int(int a, int b) {
-  while (b) {
-    const int t = a % b;
-    a = b;
-    b = t;
-  }
-  return a;
-}
-
 template <int D, int NQ>
 cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& kmap, const CUtensorMap& qmap,
                       const TcGeometry& g, cudaStream_t stream) {
@@ -805,6 +709,68 @@ cudaError_t launch_tc(const IndexerParams& p, const CUtensorMap& kmap, const CUt
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int gcd_int(int a, int b) {
+  while (b) {
+    const int t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+// Tensor maps of the indexer's operands.  Key cache: (head dim, slot in
+// page, page) with boxes of 64 dims x box_rows slots; query rows: (head dim,
+// head, row) with boxes of 64 dims x all heads x rows_per_seg rows.  Both
+// 128-byte swizzled.  False when the driver refuses the layout.
+bool encode_indexer_maps(const IndexerParams& p, int box_rows, int rows_per_seg, int q_rows,
+                         CUtensorMap* kmap, CUtensorMap* qmap) {
+  const int H = p.heads;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim),
+                                static_cast<cuuint64_t>(p.page_size),
+                                static_cast<cuuint64_t>(p.num_blocks)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.token_stride) * 2,
+                                   static_cast<cuuint64_t>(p.block_stride) * 2};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+    if (tensor_map_encoder()(kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                             const_cast<void*>(p.k_cache), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  {
+    const int64_t hs = H == 1 ? p.dim : p.q_head_stride;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(q_rows)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hs) * 2,
+                                   static_cast<cuuint64_t>(p.q_row_stride) * 2};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(H),
+                               static_cast<cuuint32_t>(rows_per_seg)};
+    if (tensor_map_encoder()(qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p.q),
+                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
+}
 
 // Whether the tensor-core indexer takes these shapes (else the mma.sync path):
 // head dim 64 / 128, page size a multiple of 8 (whole 8-row swizzle atoms per
@@ -848,37 +814,9 @@ cudaError_t launch_indexer_tc(const IndexerParams& p, cudaStream_t stream) {
   const int n = g.rows_per_seg * H;
   const int nq = n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128;
 
-  // key cache: (head dim, slot in page, page); query rows: (head dim, head, row)
   CUtensorMap kmap, qmap;
-  const cuuint32_t estr[3] = {1, 1, 1};
-  {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim),
-                                static_cast<cuuint64_t>(p.page_size),
-                                static_cast<cuuint64_t>(p.num_blocks)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.token_stride) * 2,
-                                   static_cast<cuuint64_t>(p.block_stride) * 2};
-    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(g.box_rows), 1};
-    if (tensor_map_encoder()(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
-                             const_cast<void*>(p.k_cache), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorNotSupported;
-  }
-  {
-    const int64_t hs = H == 1 ? p.dim : p.q_head_stride;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.dim), static_cast<cuuint64_t>(H),
-                                static_cast<cuuint64_t>(q_rows)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hs) * 2,
-                                   static_cast<cuuint64_t>(p.q_row_stride) * 2};
-    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(H),
-                               static_cast<cuuint32_t>(g.rows_per_seg)};
-    if (tensor_map_encoder()(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p.q),
-                             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorNotSupported;
-  }
+  if (!encode_indexer_maps(p, g.box_rows, g.rows_per_seg, q_rows, &kmap, &qmap))
+    return cudaErrorNotSupported;
   if (p.dim == 64) {
     switch (nq) {
       case 16: return launch_tc<64, 16>(p, kmap, qmap, g, stream);
