@@ -157,6 +157,44 @@ QSA_API int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_he
                        int64_t logits_row_stride, int32_t logits_width, void* stream);
 
 /*
+ * Fused decode selection: indexer scores -> top-k -> expansion in ONE launch.
+ * Replaces, for decode rows, the scoring launch + topk_expand pair of the
+ * reference's qsa_select_paged_decode (ops/indexer.py:227-279: the kernel at
+ * :24-114 fills an fp32 logits chunk, then ops/csrc/topk.cu:503-525 selects
+ * from it); the scores never leave the chip.
+ *
+ * The results are, bit for bit, those of qsa_indexer_scores (decode,
+ * query_start_loc NULL, logits_width = score_width) followed by
+ * qsa_topk_expand on those scores with lengths = each row's visible count,
+ * score_width, and the expansion arguments below.  The arguments mean what
+ * they mean in those two calls; num_sequences is the length of
+ * sequence_lengths.  scores_out (nullable, [num_rows, score_width] fp32, row
+ * stride scores_row_stride) receives the scores as qsa_indexer_scores would
+ * write them.  Returns QSA_ERR_UNSUPPORTED, launching nothing, for shapes
+ * outside the fused kernel's range (the two-call path covers them): pages
+ * not a multiple of 8 rows, a head count that is not a power of two,
+ * decode_query_len * num_heads > 32, top-k blocks above 8192, or more
+ * requests than fit the GPU at once as thread-block clusters (at most one
+ * request per SM).  The visible counts (or the positions, sequence lengths
+ * and request ids they are derived from when visible is NULL) and the page
+ * table are read before waiting on the preceding kernel of the stream (see
+ * the programmatic-dependent-launch contract in INTEGRATION.md).
+ */
+QSA_API int qsa_select_decode(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, int32_t num_heads,
+    int32_t head_dim, const void* k_cache, int64_t cache_block_stride,
+    int64_t cache_token_stride, int32_t num_blocks, int32_t page_size,
+    const int32_t* page_table, int64_t table_row_stride, int32_t table_width,
+    int32_t num_requests, const int32_t* visible, const int64_t* positions,
+    const int32_t* sequence_lengths, int32_t num_sequences, const int32_t* token_to_req,
+    int32_t ratio, int32_t decode_query_len, int32_t num_rows, const float* weights,
+    int64_t weight_row_stride, int64_t weight_head_stride, float scale, int32_t score_width,
+    const int32_t* main_table, int64_t main_table_row_stride, int32_t main_table_width,
+    int32_t main_page_size, int32_t physical, int32_t* output, int64_t output_row_stride,
+    int64_t output_col_stride, int32_t output_width, int32_t* counts, float* scores_out,
+    int64_t scores_row_stride, void* stream);
+
+/*
  * Visible compressed blocks per query row.
  * Replaces the torch computation in select_paged_tokens (reference
  * ops/indexer.py:363-369) with one launch:

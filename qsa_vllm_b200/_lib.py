@@ -38,6 +38,10 @@ SIGNATURES: dict[str, tuple] = {
         _vp, _i64, _i64, _i32, _i32, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _i32, _i32,
         _vp, _vp, _vp, _i32, _vp, _i32,
         _vp, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _f32, _vp, _i64, _i32, _vp]),
+    "qsa_select_decode": (C.c_int, [
+        _vp, _i64, _i64, _i32, _i32, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _i32, _i32,
+        _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp, _i64, _i64, _f32, _i32,
+        _vp, _i64, _i32, _i32, _i32, _vp, _i64, _i64, _i32, _vp, _vp, _i64, _vp]),
     "qsa_visible_blocks": (C.c_int, [_vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp]),
     "qsa_sparse_attention_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "qsa_sparse_attention": (C.c_int, [

@@ -355,6 +355,118 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
   return QSA_OK;
 }
 
+int qsa_select_decode(const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                      int32_t num_heads, int32_t head_dim, const void* k_cache,
+                      int64_t cache_block_stride, int64_t cache_token_stride, int32_t num_blocks,
+                      int32_t page_size, const int32_t* page_table, int64_t table_row_stride,
+                      int32_t table_width, int32_t num_requests, const int32_t* visible,
+                      const int64_t* positions, const int32_t* sequence_lengths,
+                      int32_t num_sequences, const int32_t* token_to_req, int32_t ratio,
+                      int32_t decode_query_len, int32_t num_rows, const float* weights,
+                      int64_t weight_row_stride, int64_t weight_head_stride, float scale,
+                      int32_t score_width, const int32_t* main_table,
+                      int64_t main_table_row_stride, int32_t main_table_width,
+                      int32_t main_page_size, int32_t physical, int32_t* output,
+                      int64_t output_row_stride, int64_t output_col_stride,
+                      int32_t output_width, int32_t* counts, float* scores_out,
+                      int64_t scores_row_stride, void* stream) {
+  const char* who = "qsa_select_decode";
+  if (num_rows < 0 || score_width < 0 || output_width < 0 || num_sequences < 0)
+    return fail(QSA_ERR_INVALID, "%s: negative size", who);
+  if (num_rows == 0) return QSA_OK;
+  if (!q || !k_cache || !page_table || !output || !positions || !sequence_lengths ||
+      !token_to_req)
+    return fail(QSA_ERR_INVALID, "%s: null pointer", who);
+  if (ratio <= 0) return fail(QSA_ERR_INVALID, "%s: ratio must be positive", who);
+  if (physical && (!main_table || main_page_size <= 0))
+    return fail(QSA_ERR_INVALID, "%s: physical output needs a block table and page size", who);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
+  if (page_size <= 0 || table_width < 0 || num_blocks < 0)
+    return fail(QSA_ERR_INVALID, "%s: bad page geometry", who);
+  if (!aligned(q, 16) || q_row_stride % 8 || q_head_stride % 8 || !aligned(k_cache, 16) ||
+      cache_block_stride % 8 || cache_token_stride % 8)
+    return fail(QSA_ERR_INVALID, "%s: q / key cache need 16-byte aligned rows", who);
+  if (decode_query_len <= 0 || num_rows % decode_query_len)
+    return fail(QSA_ERR_INVALID, "%s: %d decode rows not a multiple of query len %d", who,
+                num_rows, decode_query_len);
+  if (num_rows / decode_query_len > num_requests)
+    return fail(QSA_ERR_INVALID, "%s: %d decode requests but %d page-table rows", who,
+                num_rows / decode_query_len, num_requests);
+  if (scores_out && scores_row_stride < score_width)
+    return fail(QSA_ERR_INVALID, "%s: scores row stride %lld < width %d", who,
+                (long long)scores_row_stride, score_width);
+  SelectParams sp = {};
+  IndexerParams& p = sp.ix;
+  p.q = q;
+  p.q_row_stride = q_row_stride;
+  p.q_head_stride = q_head_stride;
+  p.heads = num_heads;
+  p.dim = head_dim;
+  p.k_cache = k_cache;
+  p.block_stride = cache_block_stride;
+  p.token_stride = cache_token_stride;
+  p.num_blocks = num_blocks;
+  p.page_size = page_size;
+  p.page_div = FastDiv(static_cast<uint32_t>(page_size));
+  p.table = page_table;
+  p.table_row_stride = table_row_stride;
+  p.table_width = table_width;
+  p.num_requests = num_requests;
+  p.visible = visible;
+  p.positions = positions;
+  p.seq_lens = sequence_lengths;
+  p.num_sequences = num_sequences;
+  p.token_to_req = token_to_req;
+  p.ratio = ratio;
+  p.query_start_loc = nullptr;
+  p.decode_query_len = decode_query_len;
+  p.max_query_len = decode_query_len;
+  p.query_offset = 0;
+  p.num_rows = num_rows;
+  p.weights = weights;
+  p.w_row_stride = weight_row_stride;
+  p.w_head_stride = weight_head_stride;
+  p.scale = scale;
+  p.logits = nullptr;
+  p.logits_row_stride = 0;
+  p.logits_width = score_width;
+  p.err = device_error_word();
+  TopkParams& t = sp.tk;
+  t.rows = num_rows;
+  t.width = score_width;
+  t.positions = positions;
+  t.seq_lens = sequence_lengths;
+  t.num_requests = num_sequences;
+  t.token_to_req = token_to_req;
+  t.table = main_table;
+  t.table_row_stride = main_table_row_stride;
+  t.table_width = physical ? main_table_width : 0;
+  t.output = output;
+  t.out_row_stride = output_row_stride;
+  t.out_col_stride = output_col_stride;
+  t.out_width = output_width;
+  t.counts = counts;
+  t.ratio = ratio;
+  t.page_size = physical ? main_page_size : 1;
+  t.page_div = FastDiv(static_cast<uint32_t>(t.page_size));
+  t.physical = physical ? 1 : 0;
+  t.aligned_blocks = (physical && main_page_size % ratio == 0) ? 1 : 0;
+  t.expand = 1;
+  t.topk = output_width / ratio;
+  sp.score_width = score_width;
+  sp.scores_out = scores_out;
+  sp.scores_row_stride = scores_row_stride;
+  const char* why = "unsupported shape";
+  const cudaError_t e = launch_select_decode(sp, static_cast<cudaStream_t>(stream), &why);
+  if (e == cudaErrorNotSupported)
+    return fail(QSA_ERR_UNSUPPORTED,
+                "%s: outside the fused kernel's range (%s); use qsa_indexer_scores + "
+                "qsa_topk_expand", who, why);
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  return QSA_OK;
+}
+
 int qsa_visible_blocks(const int64_t* positions, const int32_t* sequence_lengths,
                        int32_t num_requests, const int32_t* token_to_req, int32_t rows,
                        int32_t ratio, int32_t* visible, void* stream) {

@@ -299,11 +299,13 @@ namespace {
 __global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* seq_lens,
                                       int num_requests, const int32_t* token_to_req, int rows,
                                       int ratio, int32_t* visible) {
+  // Unlike the other kernels, this one lets its dependents start only after
+  // its counts are written: the next kernel may read them before its own
+  // wait, as step metadata.
   pdl_wait();
-  pdl_trigger();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
-  visible[r] = visible_of(positions, seq_lens, num_requests, token_to_req, ratio, r);
+  if (r < rows) visible[r] = visible_of(positions, seq_lens, num_requests, token_to_req, ratio, r);
+  pdl_trigger();
 }
 }  // namespace
 

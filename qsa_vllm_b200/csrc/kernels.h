@@ -84,6 +84,24 @@ cudaError_t launch_visible_blocks(const int64_t* positions, const int32_t* seq_l
                                   int num_requests, const int32_t* token_to_req, int rows,
                                   int ratio, int32_t* visible, cudaStream_t stream);
 
+// ------------------------------------------- fused decode selection
+// Indexer scores -> top-k -> expansion for decode rows in one launch
+// (select_decode.cu).  `ix` describes the scoring (decode: query_start_loc is
+// nullptr; its logits fields are unused), `tk` the selection and expansion
+// (its scores / lengths / width fields are unused: the scores stay on chip and
+// each row's length is its visible count, clipped to score_width).
+struct SelectParams {
+  IndexerParams ix;
+  TopkParams tk;
+  int score_width;          // logits columns of the two-launch path (decode bucket)
+  float* scores_out;        // optional copy of the scores, [rows, score_width]
+  int64_t scores_row_stride;
+};
+// Launches the fused kernel when the shapes allow it; returns
+// cudaErrorNotSupported, launching nothing, when they do not, with the
+// reason in *why (static string; why may be nullptr).
+cudaError_t launch_select_decode(const SelectParams& p, cudaStream_t stream, const char** why);
+
 // ------------------------------------------------------------- attention
 struct AttnParams {
   const void* q;

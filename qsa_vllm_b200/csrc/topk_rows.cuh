@@ -13,7 +13,15 @@ namespace {
 struct RowMeta {
   int seq, complete, tail_start, tail_count;
   const int32_t* trow;
+  // optional shared-memory copy of the first tcache_n entries of trow
+  const int32_t* tcache;
+  int tcache_n;
 };
+
+// Entry lp (< table width) of the row's block table.
+__device__ __forceinline__ int table_entry(const RowMeta& m, int lp) {
+  return lp < m.tcache_n ? m.tcache[lp] : __ldg(m.trow + lp);
+}
 
 // Expansion metadata of one row (topk.cu:165-180): integer division truncates
 // toward zero exactly as in the reference.
@@ -29,6 +37,8 @@ __device__ __forceinline__ RowMeta row_meta(const TopkParams& p, int row) {
   m.tail_count = pos + 1 - m.tail_start;
   m.trow = p.physical ? p.table + static_cast<int64_t>(mapped ? req : 0) * p.table_row_stride
                       : nullptr;
+  m.tcache = nullptr;
+  m.tcache_n = 0;
   return m;
 }
 
@@ -38,7 +48,7 @@ __device__ __forceinline__ int map_token(const TopkParams& p, const RowMeta& m, 
   int lp, off;
   p.page_div.divmod(token, lp, off);
   if (lp >= p.table_width) return -1;
-  const int ph = __ldg(m.trow + lp);
+  const int ph = table_entry(m, lp);
   return ph >= 0 ? ph * p.page_size + off : -1;
 }
 
@@ -49,7 +59,7 @@ __device__ __forceinline__ int block_page(const TopkParams& p, const RowMeta& m,
   if (first < 0 || first >= m.seq) return -1;
   int lp, off;
   p.page_div.divmod(first, lp, off);
-  return lp < p.table_width ? __ldg(m.trow + lp) : -1;
+  return lp < p.table_width ? table_entry(m, lp) : -1;
 }
 
 // Writes the expansion of `block` at rank `rank` (block -1 writes -1s).

@@ -122,14 +122,96 @@ def compute_visible_blocks(query_positions: torch.Tensor, sequence_lengths: torc
     return out
 
 
+_QSA_ERR_UNSUPPORTED = 2
+
+
+def select_decode_fused(q, k_cache, page_table, visible_blocks, compress_ratio, decode_query_len,
+                        out, columns, *, query_positions, sequence_lengths, token_to_req,
+                        main_block_table=None, main_page_size=1, valid_counts_out=None,
+                        weights=None, scale=None, scores_out=None) -> bool:
+    """Scores, top-k and expansion of decode rows in one launch (``qsa_select_decode``).
+
+    Same results as ``indexer_scores`` over ``columns`` logits followed by
+    ``topk_expand`` (bit for bit), without the fp32 logits round trip.
+    ``visible_blocks=None`` derives each row's count in the kernel.  Returns
+    False, having launched nothing, for shapes outside the fused kernel's
+    range; other failures raise ``QSAError``.  ``scores_out`` (optional fp32
+    ``[rows, columns]``) receives the scores as well.
+    """
+    rows = q.shape[0]
+    if rows == 0:
+        return True
+    _lib.ensure_device(q.device)
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16:
+        raise TypeError("indexer q and key cache must be bfloat16")
+    if page_table.dtype != torch.int32 or out.dtype != torch.int32:
+        raise TypeError("page_table and out must be int32")
+    if visible_blocks is not None and visible_blocks.dtype != torch.int32:
+        raise TypeError("visible_blocks must be int32")
+    if query_positions.dtype != torch.int64 or sequence_lengths.dtype != torch.int32 \
+            or token_to_req.dtype != torch.int32:
+        raise TypeError("positions int64, sequence_lengths / token_to_req int32 expected")
+    if q.stride(-1) != 1 or k_cache.stride(-1) != 1:
+        raise ValueError("q and k_cache need a unit head-dim stride")
+    w_ptr, w_rs, w_hs = None, 0, 0
+    if weights is not None:
+        if weights.dtype != torch.float32:
+            raise TypeError("weights must be float32")
+        w = weights.expand(q.shape[0], q.shape[1])
+        w_ptr, w_rs, w_hs = w.data_ptr(), w.stride(0), w.stride(1)
+    dim = q.shape[2]
+    if scale is None:
+        scale = float(np.float32(dim ** -0.5))
+    physical = main_block_table is not None
+    if physical and main_block_table.dtype != torch.int32:
+        raise TypeError("main_block_table must be int32")
+    if valid_counts_out is not None and valid_counts_out.dtype != torch.int32:
+        raise TypeError("valid_counts_out must be int32")
+    if scores_out is not None and (scores_out.dtype != torch.float32
+                                   or scores_out.stride(-1) != 1):
+        raise TypeError("scores_out must be float32 with unit column stride")
+    lib = _lib.load_library()
+    with torch.cuda.device(q.device):
+        status = lib.qsa_select_decode(
+            q.data_ptr(), q.stride(0), q.stride(1), q.shape[1], dim,
+            k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.shape[0],
+            k_cache.shape[1], page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+            page_table.shape[0], _lib.ptr(visible_blocks), query_positions.data_ptr(),
+            sequence_lengths.data_ptr(), sequence_lengths.numel(), token_to_req.data_ptr(),
+            int(compress_ratio), int(decode_query_len), rows, w_ptr, w_rs, w_hs, float(scale),
+            int(columns),
+            main_block_table.data_ptr() if physical else None,
+            main_block_table.stride(0) if physical else 0,
+            main_block_table.shape[1] if physical else 0, int(main_page_size), int(physical),
+            out.data_ptr(), out.stride(0), out.stride(1), out.shape[1],
+            _lib.ptr(valid_counts_out), _lib.ptr(scores_out),
+            scores_out.stride(0) if scores_out is not None else 0,
+            _lib.stream_ptr(q.device))
+    if status == _QSA_ERR_UNSUPPORTED:
+        return False
+    _lib.check(status, "select_decode")
+    return True
+
+
 def qsa_select_paged_decode(q, k_cache, page_table, visible_blocks, token_topk, compress_ratio,
                             decode_query_len, out, max_seq_len, *, query_positions,
                             sequence_lengths, token_to_req, main_block_table=None,
                             main_page_size=1, valid_counts_out=None, weights=None, scale=None):
-    """Score decode queries and write the expanded selection (ops/indexer.py:227-279)."""
+    """Score decode queries and write the expanded selection (ops/indexer.py:227-279).
+
+    The reference's structure: scoring into fp32 logits chunks, each followed
+    by ``topk_expand``.  (``select_decode_fused`` does both in one launch with
+    identical results; on B200 it measures slower at the benchmark shapes,
+    because its selection phase is latency-bound on the scoring CTAs, so it
+    is not the default.)
+    """
     num_requests = q.shape[0] // decode_query_len
     columns = decode_logits_columns(max_seq_len, compress_ratio,
                                     page_table.shape[1] * k_cache.shape[1])
+    if visible_blocks is None:
+        # one small launch: its counts stay in L2 for both the indexer and the top-k
+        visible_blocks = compute_visible_blocks(query_positions, sequence_lengths, token_to_req,
+                                                compress_ratio)
     requests_per_chunk = max(1, _INDEXER_WORKSPACE_BYTES // (columns * 4 * decode_query_len))
     workspace_rows = min(num_requests, requests_per_chunk) * decode_query_len
     logits_workspace = torch.empty((workspace_rows, columns), dtype=torch.float32,
@@ -219,13 +301,8 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
                           device=q.device)
     if not rows:
         return out
-    if visible_blocks is None:
-        # One small launch: the counts it writes stay in L2 for both the
-        # indexer and the top-k.  (Both kernels can also derive them per row,
-        # visible_blocks=None below, but each then pays a dependent
-        # token_to_req -> sequence_lengths load before its first real work.)
-        visible_blocks = compute_visible_blocks(query_positions, sequence_lengths, token_to_req,
-                                                compress_ratio)
+    # Without visible_blocks, each part computes its rows' counts in one small
+    # launch, whose counts stay in L2 for both the indexer and the top-k.
     if num_decode_tokens:
         qsa_select_paged_decode(
             q[:num_decode_tokens], k_cache, page_table[:num_decodes],
@@ -238,10 +315,13 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
                               if valid_counts_out is not None else None),
             weights=None if weights is None else weights[:num_decode_tokens], scale=scale)
     if num_decode_tokens < rows:
+        prefill_visible = (
+            visible_blocks[num_decode_tokens:] if visible_blocks is not None
+            else compute_visible_blocks(query_positions[num_decode_tokens:], sequence_lengths,
+                                        token_to_req[num_decode_tokens:], compress_ratio))
         qsa_select_paged_prefill(
             q[num_decode_tokens:], k_cache, page_table[num_decodes:],
-            query_start_loc[num_decodes:],
-            None if visible_blocks is None else visible_blocks[num_decode_tokens:], token_topk,
+            query_start_loc[num_decodes:], prefill_visible, token_topk,
             compress_ratio, max_query_len, out[num_decode_tokens:], max_seq_len,
             query_positions=query_positions[num_decode_tokens:],
             sequence_lengths=sequence_lengths, token_to_req=token_to_req[num_decode_tokens:],
@@ -253,4 +333,4 @@ def select_paged_tokens(q, k_cache, page_table, token_to_req, query_positions, s
 
 
 __all__ = ["compute_visible_blocks", "indexer_scores", "qsa_select_paged_decode",
-           "qsa_select_paged_prefill", "select_paged_tokens"]
+           "qsa_select_paged_prefill", "select_decode_fused", "select_paged_tokens"]

@@ -3,7 +3,8 @@
     python -m qsa_vllm_b200.profile_kernels --kernel attention --config cfg2_32k \
         --batch 16 --iters 3 [--contiguous-tables] [--time]
 
-``--kernel``: ``indexer`` | ``topk`` | ``attention`` | ``step`` (all three) |
+``--kernel``: ``indexer`` | ``topk`` | ``select`` (the fused decode
+indexer + top-k launch) | ``attention`` | ``step`` (selection and attention) |
 ``prepare`` (index-query norm/RoPE, key compression, cache writes) | ``layer``
 (``prepare`` then ``step``, the reference layer's forward).
 Inputs are the synthetic workload of ``--config`` with ``--batch`` rows (the
@@ -22,7 +23,9 @@ import json
 
 import torch
 
-from .indexer import compute_visible_blocks, indexer_scores, select_paged_tokens
+from .graph_dispatch import decode_logits_columns
+from .indexer import (compute_visible_blocks, indexer_scores, select_decode_fused,
+                      select_paged_tokens)
 from .qsa import qsa_sparse_paged_attention
 from .prepare import qsa_prepare
 from .synthetic import make_prepare_inputs, make_workload
@@ -32,7 +35,8 @@ from .topk import topk_expand
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", default="attention",
-                    choices=["indexer", "topk", "attention", "step", "prepare", "layer"])
+                    choices=["indexer", "topk", "select", "attention", "step", "prepare",
+                             "layer"])
     ap.add_argument("--config", default="cfg2_32k")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--iters", type=int, default=3)
@@ -76,6 +80,16 @@ def main() -> None:
                     main_block_table=w.block_table, main_page_size=w.page_size,
                     valid_counts_out=cnt)
 
+    def run_select():
+        columns = decode_logits_columns(w.max_seq_len, r, cols)
+        if not select_decode_fused(w.index_q, w.index_cache, w.index_table, vis, r,
+                                   w.decode_query_len, idx, columns,
+                                   query_positions=w.positions, sequence_lengths=w.seq_lens,
+                                   token_to_req=w.token_to_req, main_block_table=w.block_table,
+                                   main_page_size=w.page_size, valid_counts_out=cnt,
+                                   weights=w.index_weights, scale=w.index_scale):
+            raise SystemExit("the fused selection declined this workload")
+
     def run_attention():
         qsa_sparse_paged_attention(w.q, w.k_cache, w.v_cache, idx, w.block_table, w.token_to_req,
                                    out, output_gate=w.gate, use_decode_kernel=True,
@@ -104,7 +118,8 @@ def main() -> None:
 
     run_indexer()
     run_topk()
-    fn = {"indexer": run_indexer, "topk": run_topk, "attention": run_attention,
+    fn = {"indexer": run_indexer, "topk": run_topk, "select": run_select,
+          "attention": run_attention,
           "step": run_step, "prepare": run_prepare, "layer": run_layer}[a.kernel]
     for _ in range(a.warmup):
         fn()
