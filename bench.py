@@ -463,6 +463,8 @@ def main() -> None:
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "value_note": "value = all ranks' rows / max-over-ranks step time (whole job)",
+        "per_gpu": {"value": value / world, "unit": "tokens/s per GPU"},
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {**workload_desc(args.config, w),
                    "parallelism": f"tp{world} head-sharded (indexer replicated)"},

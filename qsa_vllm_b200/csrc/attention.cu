@@ -578,29 +578,42 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
 // Merge of the partial (normalized O, LSE) slots of every (row, query head):
 // the reference's split-K merge (ops/qsa.py:306-362) over the per-warp
 // partials of all splits, then bf16 rounding and the optional sigmoid gate.
-// One block per (row, 8 query heads), one warp per head, D/32 dims per lane;
-// the partial loop is unrolled so several slots' loads are in flight.
-constexpr int kMergeHeads = 8;
-template <int D>
-__global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParams p) {
-  constexpr int DPL = D / 32;  // dims per lane
+// A block of 8 warps serves one row and 8 / W query heads, W warps per head
+// (W = 1, 2, 4 or 8 from the plan's most partial slots per head), D/32 dims
+// per lane.  Warp w of a head takes the batches of 8 slots w, w + W, ...;
+// every slot's LSE and partial of a batch are loaded before any is used, so
+// with at most 8 W slots per head (the planner's common case) the merge is
+// one memory round trip.  The W running (max, sum, O) states of a head are
+// then combined through shared memory.
+constexpr int kMergeWarps = 8;
+template <int D, int W>
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const AttnParams p) {
+  constexpr int DPL = D / 32;               // dims per lane
+  constexpr int kHeads = kMergeWarps / W;   // heads per block
+  __shared__ float st_o[W > 1 ? kMergeWarps : 1][32 * DPL];
+  __shared__ float st_m[kMergeWarps], st_d[kMergeWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hl = warp / W, w = warp % W;
   const int row = blockIdx.x;
-  const int head = blockIdx.y * kMergeHeads + (threadIdx.x >> 5);
-  if (head >= p.q_heads) return;
-  const int d0 = (threadIdx.x & 31) * DPL;
+  const int head = blockIdx.y * kHeads + hl;
+  const bool live = head < p.q_heads;
+  const int d0 = lane * DPL;
   const int64_t slot_stride = static_cast<int64_t>(p.rows) * p.q_heads;
-  const int64_t base = static_cast<int64_t>(row) * p.q_heads + head;
+  const int64_t base = static_cast<int64_t>(row) * p.q_heads + (live ? head : 0);
   // partial slots of this head: slot_group per CTA whose range met its pair
   const int groups = p.kv_heads / p.heads_per_unit;
-  const int hg = (head / (p.q_heads / p.kv_heads)) / p.heads_per_unit;
+  const int hg = ((live ? head : 0) / (p.q_heads / p.kv_heads)) / p.heads_per_unit;
   const int64_t first = (static_cast<int64_t>(row) * groups + hg) * p.pair_tiles;
-  const int P = (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) * p.slot_group;
+  const int P = live ? (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) *
+                           p.slot_group
+                     : 0;
   // the gate does not depend on the partials: its loads go out first
   float gv[DPL];
-  const __nv_bfloat16* gp = p.gate == nullptr ? nullptr
-                            : static_cast<const __nv_bfloat16*>(p.gate) +
-                                  static_cast<int64_t>(row) * p.gate_row_stride +
-                                  static_cast<int64_t>(head) * p.gate_head_stride;
+  const __nv_bfloat16* gp = (p.gate == nullptr || !live || w != 0)
+                                ? nullptr
+                                : static_cast<const __nv_bfloat16*>(p.gate) +
+                                      static_cast<int64_t>(row) * p.gate_row_stride +
+                                      static_cast<int64_t>(head) * p.gate_head_stride;
 #pragma unroll
   for (int i = 0; i < DPL; ++i)
     gv[i] = gp != nullptr ? __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride])
@@ -613,10 +626,8 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
   float acc[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  // 8 slots per batch: every slot's LSE and partial are loaded before any is
-  // used; with at most 8 slots (the common case) that is the only round trip.
   float M = -INFINITY;
-  for (int s0 = 0; s0 < P; s0 += 8) {
+  for (int s0 = 8 * w; s0 < P; s0 += 8 * W) {
     float lse[8];
     float v[8][DPL];
 #pragma unroll
@@ -648,12 +659,41 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
     M = m_new;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float w = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
-      den += w;
+      const float wt = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
+      den += wt;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * w;
+      for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * wt;
     }
   }
+  if constexpr (W > 1) {
+    // combine the head's W warp states in warp w == 0
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) st_o[warp][d0 + i] = acc[i];
+    if (lane == 0) {
+      st_m[warp] = M;
+      st_d[warp] = den;
+    }
+    __syncthreads();
+    if (w == 0) {
+      float Mt = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < W; ++k) Mt = fmaxf(Mt, st_m[warp + k]);
+      den = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      if (Mt != -INFINITY) {
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+          const float mk = st_m[warp + k];
+          const float sc = mk == -INFINITY ? 0.f : exp2f(mk - Mt);
+          den += st_d[warp + k] * sc;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] += st_o[warp + k][d0 + i] * sc;
+        }
+      }
+    }
+  }
+  if (!live || w != 0) return;
   const float inv = den > 0.f ? 1.f / den : 0.f;
   __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
                       static_cast<int64_t>(row) * p.out_row_stride +
@@ -666,6 +706,23 @@ __global__ void __launch_bounds__(kMergeHeads * 32) merge_kernel(const AttnParam
       o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-gv[i + 1]));
     }
     *reinterpret_cast<__nv_bfloat162*>(op + i) = __floats2bfloat162_rn(o0, o1);
+  }
+}
+
+// Warps per head of the merge: enough batches of 8 slots for the plan's
+// most partial slots of a head, at most 8.
+template <int D>
+cudaError_t launch_merge(const AttnParams& p, cudaStream_t stream) {
+  const int batches = (p.partials + 7) / 8;
+  const int W = batches <= 1 ? 1 : batches <= 2 ? 2 : batches <= 4 ? 4 : 8;
+  const dim3 block(kMergeWarps * 32);
+  const unsigned heads_per_block = static_cast<unsigned>(kMergeWarps / W);
+  const dim3 grid(p.rows, (p.q_heads + heads_per_block - 1) / heads_per_block);
+  switch (W) {
+    case 1: return count_launches(launch_kernel(merge_kernel<D, 1>, grid, block, 0, stream, 1, p));
+    case 2: return count_launches(launch_kernel(merge_kernel<D, 2>, grid, block, 0, stream, 1, p));
+    case 4: return count_launches(launch_kernel(merge_kernel<D, 4>, grid, block, 0, stream, 1, p));
+    default: return count_launches(launch_kernel(merge_kernel<D, 8>, grid, block, 0, stream, 1, p));
   }
 }
 
@@ -682,9 +739,7 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
       launch_kernel(attention_kernel<D, NT, HB>, dim3(grid), dim3(kThreads), smem, stream, 1, p));
   if (e != cudaSuccess) return e;
   record_attention_event(1, stream);
-  return count_launches(launch_kernel(
-      merge_kernel<D>, dim3(p.rows, (p.q_heads + kMergeHeads - 1) / kMergeHeads),
-      dim3(kMergeHeads * 32), 0, stream, 1, p));
+  return launch_merge<D>(p, stream);
 }
 
 template <int D, int NT>
