@@ -42,6 +42,9 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--contiguous-tables", action="store_true")
+    ap.add_argument("--shard", type=int, nargs=2, metavar=("TP", "RANK"), default=None,
+                    help="one rank's head share under tensor parallelism TP (as the "
+                         "multi-GPU benchmark shards): H_q/TP query heads, its KV head(s)")
     ap.add_argument("--time", action="store_true")
     ap.add_argument("--visible-kernel", action="store_true",
                     help="step: compute visible counts with qsa_visible_blocks first and "
@@ -49,6 +52,8 @@ def main() -> None:
     a = ap.parse_args()
     dev = torch.device("cuda")
     w = make_workload(a.config, device=dev, seed=0, batch=a.batch)
+    if a.shard is not None:
+        w = w.shard_heads(*a.shard)
     if a.contiguous_tables:
         for name in ("block_table", "index_table"):
             t = getattr(w, name)
@@ -145,7 +150,7 @@ def main() -> None:
         e.record()
     torch.cuda.synchronize()
     ms = [s.elapsed_time(e) for s, e in ev]
-    print(json.dumps({"kernel": a.kernel, "config": a.config, "rows": rows,
+    print(json.dumps({"kernel": a.kernel, "config": a.config, "rows": rows, "shard": a.shard,
                       "contiguous_tables": a.contiguous_tables, "ms_min": min(ms),
                       "ms_median": sorted(ms)[len(ms) // 2]}))
 
