@@ -30,9 +30,13 @@
 //    group as N (no padding lanes at group 8), in two independent
 //    accumulator chains; P^T is transposed in registers (movmatrix) into the
 //    B operand of O^T = V^T.P^T.
-//  * Per-warp softmax states are merged in shared memory at the end of a
-//    unit; with more than one split, fp32 partials + LSE go to the caller's
-//    workspace and a small merge kernel finishes (the reference's layout).
+//  * At the end of a pair the softmax states of the warps that share a KV
+//    head are folded together in shared memory.  A pair met by one CTA only
+//    (the common case at prefill) is finished there: normalised, rounded to
+//    bf16, gated and stored.  A range boundary inside a pair splits it:
+//    each piece writes a normalised fp32 partial + LSE (the reference's
+//    split-K format) and a small merge kernel combines the at most
+//    sk_ctas - 1 split pairs.
 #include <algorithm>
 #include <cmath>
 
@@ -74,7 +78,12 @@ struct Smem {
   static __device__ __forceinline__ int tok_off(int j) { return (j >> 2) * kBlk + (j & 3) * kRow; }
   alignas(128) uint8_t stage[kStages][(kTT / 4) * kBlk];
   alignas(128) uint8_t q[2][kQRows * 2 * D];
-  int32_t ring[kProducers][kRing][64];
+  int32_t ring[kProducers][kRing][kTT];
+  // unit-end fold of the warps' softmax states (4 writer slots of one
+  // m16n8 column block: (D/16) float4 per lane), reused as the pair's
+  // [head][dim] fp32 result (at most 32 heads)
+  alignas(16) float comb[32 * D];
+  float cm[4][8], cl[4][8];  // writer slot: m and l of its 8 head columns
   uint64_t mask[kStages];
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -84,7 +93,7 @@ struct Smem {
 };
 
 struct Unit {
-  int row, hg, split, t0, t1, n_cols;
+  int row, hg, pieces, t0, t1, n_cols;  // pieces: CTAs whose ranges meet the pair
 };
 
 // Stream-K split: CTA c owns units [U*c/C, U*(c+1)/C) of the U = pairs x
@@ -116,7 +125,7 @@ __device__ __forceinline__ Unit unit_of(const AttnParams& p, int groups, int64_t
   const int t1 = static_cast<int>(min(ub, first + T) - first);
   x.t1 = min(t1, tiles);
   x.t0 = min(t0, x.t1);
-  x.split = static_cast<int>(blockIdx.x) - sk_owner(p, first);
+  x.pieces = sk_owner(p, first + T - 1) - sk_owner(p, first) + 1;
   return x;
 }
 
@@ -130,6 +139,73 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
                "r"(valid ? 4 : 0)
                : "memory");
+}
+
+// Per KV head of a finished pair, its GQA group's output in 8-dim chunks
+// spread over the 8 / HB consumer warps that share the head.
+template <int D, int HB, int NT>
+constexpr int kOutItems = (8 * NT * (D / 8) + (8 / HB) * 32 - 1) / ((8 / HB) * 32);
+
+// Gate values of dims d0..d0+7 of one (row, head), packed bf16 pairs.  The
+// loads are volatile asm so they stay where they are issued (a unit's start)
+// instead of being moved next to their use at the unit's end.
+__device__ __forceinline__ uint4 load_gate8(const AttnParams& p, int row, int head, int d0) {
+  const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) +
+                            static_cast<int64_t>(row) * p.gate_row_stride +
+                            static_cast<int64_t>(head) * p.gate_head_stride;
+  uint4 r;
+  if (p.gate_vec) {
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(gp + d0));
+    return r;
+  }
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    unsigned short v;
+    asm volatile("ld.global.nc.u16 %0, [%1];"
+                 : "=h"(v)
+                 : "l"(gp + static_cast<int64_t>(d0 + i) * p.gate_dim_stride));
+    w[i] = v;
+  }
+  r.x = w[0] | (w[1] << 16);
+  r.y = w[2] | (w[3] << 16);
+  r.z = w[4] | (w[5] << 16);
+  r.w = w[6] | (w[7] << 16);
+  return r;
+}
+
+// 1 / (1 + e^-x) with the fast exponential and division: a few ulp of fp32,
+// far below the bf16 rounding of the gated output.
+__device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// Output dims d0..d0+7 of one (row, head): bf16 rounding; with a gate,
+// bf16(o) * sigmoid(gate) rounded again (ops/qsa.py:250-275, :348-358).
+__device__ __forceinline__ void store_out8(const AttnParams& p, int row, int head, int d0,
+                                           float4 a, float4 b, uint4 gate8) {
+  float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  if (p.gate != nullptr) {
+    const uint32_t gw[4] = {gate8.x, gate8.y, gate8.z, gate8.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float g0 = __uint_as_float(gw[i] << 16), g1 = __uint_as_float(gw[i] & 0xffff0000u);
+      v[2 * i] = __bfloat162float(__float2bfloat16_rn(v[2 * i])) * sigmoid(g0);
+      v[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(v[2 * i + 1])) * sigmoid(g1);
+    }
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
+                      static_cast<int64_t>(row) * p.out_row_stride +
+                      static_cast<int64_t>(head) * p.out_head_stride + d0;
+  if (p.out_vec) {
+    *reinterpret_cast<uint4*>(op) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<uint32_t*>(op)[i] = w[i];
+  }
 }
 
 // Iterator over this CTA's (unit, tile) positions: the producer uses one to
@@ -181,7 +257,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   const uint8_t* vbase = static_cast<const uint8_t*>(p.v_cache);
   const uint8_t* qbase = static_cast<const uint8_t*>(p.q);
   const int pw = (threadIdx.x >> 5) - kConsumerWarps;  // this producer fills it % kProducers == pw
-  int32_t (*ring)[64] = sm.ring[pw];
+  int32_t (*ring)[TT] = sm.ring[pw];
 
   Cursor<TT> ahead;  // this producer's own tiles: positions pw, pw + kProducers, ...
   ahead.init(p, units, groups, ua, ub);
@@ -390,9 +466,36 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   // reaches every named barrier, so no warp of the CTA is left waiting at one.
   bool aborted = false;
   int it = 0, k = 0;
+  const int hqp = HB * group;  // query heads of a pair
+  // The R = 8 / HB warps sharing KV head hh.
+  constexpr int R = kGroups * SUB;
+  constexpr int kItems = kOutItems<D, HB, NT>;
+  const int head0 = hh * group;  // first query head of hh within the pair
   for (; k < units; ++k) {
     const Unit x = unit_of<TT>(p, groups, ua, ub, k);
     const int qb = k & 1;
+    // Rank j of this warp among the head's R warps for the unit-end fold:
+    // the group that takes the unit's last tile (and so finishes last) ranks
+    // above the other, so in the first folding round it only stores its
+    // state and the warps that finished earlier do the folding.  tr: thread
+    // rank.
+    const int lastg = (it + max(x.t1 - x.t0, 1) - 1) % kGroups;
+    const int j = (cg == lastg ? SUB : 0) + sub;
+    const int tr = j * 32 + lane;
+    // The gate chunks this thread stores at the unit's end, loaded now so
+    // their latency hides behind the unit's tiles.
+    uint4 gpre[kItems];
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) gpre[i] = make_uint4(0, 0, 0, 0);
+    if (p.gate != nullptr && x.pieces == 1) {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int item = tr + i * R * 32;
+        if (item < group * (D / 8))
+          gpre[i] = load_gate8(p, x.row, x.hg * hqp + head0 + item / (D / 8),
+                               (item % (D / 8)) * 8);
+      }
+    }
     aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
     if (!aborted && !mbar_wait(&sm.qfull[qb], (k >> 1) & 1)) {
       record_error(p.err, kDeviceErrWaitTimeout);
@@ -503,13 +606,15 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
     }
 
-    // ---- this warp's partial: normalized O and LSE of its heads over its
-    // tokens of the unit, written straight from registers (base-2 LSE, the
-    // reference's split-K format).  The merge kernel combines the partials of
-    // all (split, group, sub-tile) slots of a head.
-    // An aborted launch still writes this warp's slots, as empty partials
-    // (O = 0, LSE = -inf): the merge gives them no weight and never combines
-    // values that another call left in the workspace.
+    // ---- unit end: fold the softmax states of the R warps sharing a KV
+    // head by halving.  Each head has its own shared-memory region (32 D / HB
+    // floats: R / 2 exchange slots of (D / 16) float4 per lane, later its
+    // GQA group's [head][dim] result) and its own named barrier, so heads do
+    // not wait for each other.  Round 1: warp j >= R/2 stores its (O, m, l)
+    // in slot j - R/2 and warp j - R/2 folds it in; later rounds: warp j in
+    // [half, 2 half) stores in its own slot j, the one it read last round
+    // (no one else reads it), and warp j - half folds it in.  All warps of
+    // a head meet every barrier (aborted warps fold in an empty state).
     aborted = __any_sync(0xffffffffu, aborted);
     if (aborted) {
 #pragma unroll
@@ -520,28 +625,113 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
           o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
       }
     }
-    const int pslot = (x.split * kGroups + cg) * SUB + sub;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {  // l over the warp's 16 token rows
+        l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 4);
+        l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 8);
+        l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 16);
+      }
+    float* region = sm.comb + hh * (32 * D / HB);
+    float4* slots4 = reinterpret_cast<float4*>(region);
+    const int bar_id = 1 + hh, bar_n = R * 32;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
+      // region free: the head's warps are done with its previous contents
+      named_barrier(bar_id, bar_n);
 #pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        float lv = l[nt][hc];
-        lv += __shfl_xor_sync(0xffffffffu, lv, 4);
-        lv += __shfl_xor_sync(0xffffffffu, lv, 8);
-        lv += __shfl_xor_sync(0xffffffffu, lv, 16);
-        const int hl = 8 * nt + 2 * t4 + hc;
-        if (hl >= group) continue;
-        const bool has = lv > 0.f;
-        const float inv = has ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
-        const int head = (x.hg * HB + hh) * group + hl;
-        const int64_t base = (static_cast<int64_t>(pslot) * p.rows + x.row) * p.q_heads + head;
-        float* po = p.part_o + base * D;
+      for (int half = R / 2; half >= 1; half >>= 1) {
+        if (j >= half && j < 2 * half) {
+          const int slot = half == R / 2 ? j - half : j;
+          const int cs = hh * (R / 2) + slot;  // the pair's m/l slot
+          __syncwarp();
 #pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          po[mt * 16 + g] = o[mt][nt][hc] * inv;
-          po[mt * 16 + g + 8] = o[mt][nt][2 + hc] * inv;
+          for (int mt = 0; mt < KS; ++mt)
+            slots4[(slot * KS + mt) * 32 + lane] =
+                make_float4(o[mt][nt][0], o[mt][nt][1], o[mt][nt][2], o[mt][nt][3]);
+          if (g == 0) {
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              sm.cm[cs][2 * t4 + hc] = m[nt][hc];
+              sm.cl[cs][2 * t4 + hc] = l[nt][hc];
+            }
+          }
         }
-        if (g == 0) p.part_lse[base] = has ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
+        named_barrier(bar_id, bar_n);
+        if (j < half) {
+          const int slot = half == R / 2 ? j : j + half;
+          const int cs = hh * (R / 2) + slot;
+          float sa[2], sb[2];
+#pragma unroll
+          for (int hc = 0; hc < 2; ++hc) {
+            const float m2 = sm.cm[cs][2 * t4 + hc];
+            const float mx = fmaxf(m[nt][hc], m2);
+            sa[hc] = fast_exp2(m[nt][hc] - mx);
+            sb[hc] = fast_exp2(m2 - mx);
+            l[nt][hc] = l[nt][hc] * sa[hc] + sm.cl[cs][2 * t4 + hc] * sb[hc];
+            m[nt][hc] = mx;
+          }
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            const float4 t = slots4[(slot * KS + mt) * 32 + lane];
+            o[mt][nt][0] = o[mt][nt][0] * sa[0] + t.x * sb[0];
+            o[mt][nt][1] = o[mt][nt][1] * sa[1] + t.y * sb[1];
+            o[mt][nt][2] = o[mt][nt][2] * sa[0] + t.z * sb[0];
+            o[mt][nt][3] = o[mt][nt][3] * sa[1] + t.w * sb[1];
+          }
+        }
+      }
+    }
+    // ---- the head's result, staged in its region as [q head][dim] fp32
+    // (8-float chunks XOR-swizzled by head: conflict-free fragment stores,
+    // 16-byte reads).  A pair this CTA met whole is stored as bf16 output
+    // with the gate (ops/qsa.py:250-275); a piece of a split pair as a
+    // normalised fp32 partial and its base-2 LSE in slot
+    // 2 * cta + (first pair met ? 0 : 1).
+    const bool whole = x.pieces == 1;
+    const int pslot = 2 * static_cast<int>(blockIdx.x) + (k == 0 ? 0 : 1);
+    named_barrier(bar_id, bar_n);
+    if (j == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          const int hl = 8 * nt + 2 * t4 + hc;
+          if (hl >= group) continue;
+          const float lv = l[nt][hc];
+          const float inv = lv > 0.f ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
+          float* srow = region + hl * D;
+          const int sw = (hl >> 1) & 3;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            srow[(((2 * mt) ^ sw) << 3) + g] = o[mt][nt][hc] * inv;
+            srow[(((2 * mt + 1) ^ sw) << 3) + g] = o[mt][nt][2 + hc] * inv;
+          }
+          if (!whole && g == 0)
+            p.part_lse[static_cast<int64_t>(pslot) * hqp + head0 + hl] =
+                lv > 0.f ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
+        }
+      }
+    }
+    named_barrier(bar_id, bar_n);
+    if (whole) {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int item = tr + i * R * 32;
+        if (item >= group * (D / 8)) continue;
+        const int hl = item / (D / 8), c = item % (D / 8);
+        const float4* src =
+            reinterpret_cast<const float4*>(region + hl * D + ((c ^ ((hl >> 1) & 3)) << 3));
+        store_out8(p, x.row, x.hg * hqp + head0 + hl, c * 8, src[0], src[1], gpre[i]);
+      }
+    } else {
+      float4* po = reinterpret_cast<float4*>(p.part_o +
+                                             (static_cast<int64_t>(pslot) * hqp + head0) * D);
+      for (int item = tr; item < group * (D / 4); item += R * 32) {
+        const int hl = item / (D / 4), c4 = item % (D / 4);
+        po[item] = *reinterpret_cast<const float4*>(
+            region + hl * D + (((c4 >> 1) ^ ((hl >> 1) & 3)) << 3) + (c4 & 1) * 4);
       }
     }
   }
@@ -575,100 +765,88 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
     consumer<D, NT, HB>(p, sm, units, groups, ua, ub);
 }
 
-// Merge of the partial (normalized O, LSE) slots of every (row, query head):
-// the reference's split-K merge (ops/qsa.py:306-362) over the per-warp
-// partials of all splits, then bf16 rounding and the optional sigmoid gate.
-// A block of 8 warps serves one row and 8 / W query heads, W warps per head
-// (W = 1, 2, 4 or 8 from the plan's most partial slots per head), D/32 dims
-// per lane.  Warp w of a head takes the batches of 8 slots w, w + W, ...;
-// every slot's LSE and partial of a batch are loaded before any is used, so
-// with at most 8 W slots per head (the planner's common case) the merge is
-// one memory round trip.  The W running (max, sum, O) states of a head are
-// then combined through shared memory.
-constexpr int kMergeWarps = 8;
+// Merge of the split pairs: the reference's split-K merge (ops/qsa.py:306-362)
+// over the pieces of each pair that a range boundary cuts.  Block column x
+// takes the pair that CTA b = split_cta[x]'s range ends in (b holds the pair's
+// first tile and a later CTA its last), so each split pair has one block
+// column (grid.y blocks cover its heads).  The pieces are the partial slots
+// of CTAs o1..o2:
+// 2*o1 + 1 (2*o1 when o1's range starts at the pair), then 2*c for the later
+// CTAs, for which it is the first pair met.  Weights 2^(lse - max lse); bf16
+// rounding and the optional sigmoid gate follow.  A block of 8 warps serves
+// 8 / W heads of the pair, W warps per head (from the plan's most pieces of
+// a pair, so that each warp loads one batch of 4 pieces in the common case);
+// a lane holds 4 dims.  The W states of a head are combined in shared memory.
+constexpr int kMergeThreads = 256;
 template <int D, int W>
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const AttnParams p) {
-  constexpr int DPL = D / 32;               // dims per lane
-  constexpr int kHeads = kMergeWarps / W;   // heads per block
-  __shared__ float st_o[W > 1 ? kMergeWarps : 1][32 * DPL];
-  __shared__ float st_m[kMergeWarps], st_d[kMergeWarps];
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p) {
+  constexpr int kHeads = 8 / W;  // heads per block
+  __shared__ float4 st_o[W > 1 ? 8 : 1][32];
+  __shared__ float st_m[8], st_d[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hl = warp / W, w = warp % W;
-  const int row = blockIdx.x;
-  const int head = blockIdx.y * kHeads + hl;
-  const bool live = head < p.q_heads;
-  const int d0 = lane * DPL;
-  const int64_t slot_stride = static_cast<int64_t>(p.rows) * p.q_heads;
-  const int64_t base = static_cast<int64_t>(row) * p.q_heads + (live ? head : 0);
-  // partial slots of this head: slot_group per CTA whose range met its pair
+  const int b = p.split_cta[blockIdx.x];
+  const int64_t T = p.pair_tiles;
+  const int64_t pair = (sk_begin(p, b + 1) - 1) / T;
+  const int64_t first = pair * T;
+  const int o1 = b, o2 = sk_owner(p, first + T - 1);
+  const int group = p.q_heads / p.kv_heads;
+  const int hqp = p.heads_per_unit * group;
+  const int h = static_cast<int>(blockIdx.y) * kHeads + hl;  // head within the pair
+  const bool live = h < hqp && lane < D / 4;
   const int groups = p.kv_heads / p.heads_per_unit;
-  const int hg = ((live ? head : 0) / (p.q_heads / p.kv_heads)) / p.heads_per_unit;
-  const int64_t first = (static_cast<int64_t>(row) * groups + hg) * p.pair_tiles;
-  const int P = live ? (sk_owner(p, first + p.pair_tiles - 1) - sk_owner(p, first) + 1) *
-                           p.slot_group
-                     : 0;
-  // the gate does not depend on the partials: its loads go out first
-  float gv[DPL];
-  const __nv_bfloat16* gp = (p.gate == nullptr || !live || w != 0)
-                                ? nullptr
-                                : static_cast<const __nv_bfloat16*>(p.gate) +
-                                      static_cast<int64_t>(row) * p.gate_row_stride +
-                                      static_cast<int64_t>(head) * p.gate_head_stride;
+  const int row = static_cast<int>(pair / groups), hg = static_cast<int>(pair % groups);
+  const int d0 = lane * 4;
+  // the gate is a step input the attention kernel does not write: its loads
+  // go out before waiting on that kernel
+  float gv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (live && w == 0 && p.gate != nullptr) {
+    const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) +
+                              static_cast<int64_t>(row) * p.gate_row_stride +
+                              static_cast<int64_t>(hg * hqp + h) * p.gate_head_stride;
 #pragma unroll
-  for (int i = 0; i < DPL; ++i)
-    gv[i] = gp != nullptr ? __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride])
-                          : 0.f;
-  // The gate is a step input that the attention kernel does not write: it is
-  // read above, before waiting on that kernel; its partials are read below.
+    for (int i = 0; i < 4; ++i)
+      gv[i] = __bfloat162float(gp[static_cast<int64_t>(d0 + i) * p.gate_dim_stride]);
+  }
   pdl_wait();
   pdl_trigger();
-  float den = 0.f;
-  float acc[DPL];
+  const int P = o2 - o1 + 1;
+  const int e1 = sk_begin(p, o1) == first ? 0 : 1;
+  float M = -INFINITY, den = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i0 = 4 * w; live && i0 < P; i0 += 4 * W) {
+    float lse[4];
+    float4 v[4];
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  float M = -INFINITY;
-  for (int s0 = 8 * w; s0 < P; s0 += 8 * W) {
-    float lse[8];
-    float v[8][DPL];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t b = (s0 + j < P ? s0 + j : 0) * slot_stride + base;
-      lse[j] = s0 + j < P ? __ldg(p.part_lse + b) : -INFINITY;
-      const float* po = p.part_o + b * D + d0;
-      if constexpr (DPL == 4) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(po));
-        v[j][0] = t.x;
-        v[j][1] = t.y;
-        v[j][2] = t.z;
-        v[j][3] = t.w;
-      } else {
-        const float2 t = __ldg(reinterpret_cast<const float2*>(po));
-        v[j][0] = t.x;
-        v[j][1] = t.y;
-      }
+    for (int jj = 0; jj < 4; ++jj) {
+      const int i = i0 + jj;
+      const int64_t slot = i == 0 ? 2 * o1 + e1 : 2 * static_cast<int64_t>(o1 + i);
+      const int64_t base = i < P ? slot * hqp + h : 0;
+      lse[jj] = i < P ? __ldg(p.part_lse + base) : -INFINITY;
+      v[jj] = i < P ? __ldg(reinterpret_cast<const float4*>(p.part_o + base * D + d0))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float m_new = M;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) m_new = fmaxf(m_new, lse[j]);
-    if (m_new == -INFINITY) continue;  // no valid slot yet
-    // rescale what earlier batches accumulated to the new maximum
+    for (int jj = 0; jj < 4; ++jj) m_new = fmaxf(m_new, lse[jj]);
+    if (m_new == -INFINITY) continue;  // no valid piece yet
     const float r = M == -INFINITY ? 0.f : exp2f(M - m_new);
     den *= r;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] *= r;
+    for (int c = 0; c < 4; ++c) acc[c] *= r;
     M = m_new;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float wt = exp2f(lse[j] - M);  // 0 for unused slots (lse -inf)
+    for (int jj = 0; jj < 4; ++jj) {
+      const float wt = exp2f(lse[jj] - M);  // 0 for empty pieces
       den += wt;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] += v[j][i] * wt;
+      acc[0] += v[jj].x * wt;
+      acc[1] += v[jj].y * wt;
+      acc[2] += v[jj].z * wt;
+      acc[3] += v[jj].w * wt;
     }
   }
   if constexpr (W > 1) {
-    // combine the head's W warp states in warp w == 0
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) st_o[warp][d0 + i] = acc[i];
+    st_o[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     if (lane == 0) {
       st_m[warp] = M;
       st_d[warp] = den;
@@ -679,45 +857,48 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const AttnParam
 #pragma unroll
       for (int k = 0; k < W; ++k) Mt = fmaxf(Mt, st_m[warp + k]);
       den = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       if (Mt != -INFINITY) {
 #pragma unroll
         for (int k = 0; k < W; ++k) {
           const float mk = st_m[warp + k];
           const float sc = mk == -INFINITY ? 0.f : exp2f(mk - Mt);
+          const float4 t = st_o[warp + k][lane];
           den += st_d[warp + k] * sc;
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[i] += st_o[warp + k][d0 + i] * sc;
+          acc[0] += t.x * sc;
+          acc[1] += t.y * sc;
+          acc[2] += t.z * sc;
+          acc[3] += t.w * sc;
         }
       }
     }
   }
   if (!live || w != 0) return;
   const float inv = den > 0.f ? 1.f / den : 0.f;
-  __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) +
-                      static_cast<int64_t>(row) * p.out_row_stride +
-                      static_cast<int64_t>(head) * p.out_head_stride + d0;
+  float o[4];
 #pragma unroll
-  for (int i = 0; i < DPL; i += 2) {
-    float o0 = acc[i] * inv, o1 = acc[i + 1] * inv;
-    if (gp != nullptr) {
-      o0 = __bfloat162float(__float2bfloat16_rn(o0)) / (1.f + __expf(-gv[i]));
-      o1 = __bfloat162float(__float2bfloat16_rn(o1)) / (1.f + __expf(-gv[i + 1]));
-    }
-    *reinterpret_cast<__nv_bfloat162*>(op + i) = __floats2bfloat162_rn(o0, o1);
+  for (int c = 0; c < 4; ++c) {
+    o[c] = acc[c] * inv;
+    if (p.gate != nullptr)
+      o[c] = __bfloat162float(__float2bfloat16_rn(o[c])) * sigmoid(gv[c]);
   }
+  uint32_t* op = reinterpret_cast<uint32_t*>(
+      static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.out_row_stride +
+      static_cast<int64_t>(hg * hqp + h) * p.out_head_stride + d0);
+  op[0] = pack_bf16x2(o[0], o[1]);
+  op[1] = pack_bf16x2(o[2], o[3]);
 }
 
-// Warps per head of the merge: enough batches of 8 slots for the plan's
-// most partial slots of a head, at most 8.
+// W warps per head: enough batches of 4 pieces for the plan's most pieces
+// of a split pair, at most 8.
 template <int D>
 cudaError_t launch_merge(const AttnParams& p, cudaStream_t stream) {
-  const int batches = (p.partials + 7) / 8;
+  const int batches = (p.merge_pieces + 3) / 4;
   const int W = batches <= 1 ? 1 : batches <= 2 ? 2 : batches <= 4 ? 4 : 8;
-  const dim3 block(kMergeWarps * 32);
-  const unsigned heads_per_block = static_cast<unsigned>(kMergeWarps / W);
-  const dim3 grid(p.rows, (p.q_heads + heads_per_block - 1) / heads_per_block);
+  const int hqp = p.heads_per_unit * (p.q_heads / p.kv_heads);
+  const int heads_per_block = 8 / W;
+  const dim3 grid(p.n_split, (hqp + heads_per_block - 1) / heads_per_block);
+  const dim3 block(kMergeThreads);
   switch (W) {
     case 1: return count_launches(launch_kernel(merge_kernel<D, 1>, grid, block, 0, stream, 1, p));
     case 2: return count_launches(launch_kernel(merge_kernel<D, 2>, grid, block, 0, stream, 1, p));
@@ -728,6 +909,8 @@ cudaError_t launch_merge(const AttnParams& p, cudaStream_t stream) {
 
 template <int D, int NT, int HB>
 cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
+  static_assert(sizeof(Smem<D, NT, HB>) <= 227 * 1024, "shared memory above the opt-in limit");
+  static_assert(HB * 8 * NT <= 32, "a pair's heads exceed the unit-end buffer");
   const size_t smem = sizeof(Smem<D, NT, HB>);
   cudaError_t e = set_attr_once(reinterpret_cast<const void*>(attention_kernel<D, NT, HB>),
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -739,6 +922,7 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
       launch_kernel(attention_kernel<D, NT, HB>, dim3(grid), dim3(kThreads), smem, stream, 1, p));
   if (e != cudaSuccess) return e;
   record_attention_event(1, stream);
+  if (p.partials == 0) return cudaSuccess;  // no pair is split
   return launch_merge<D>(p, stream);
 }
 
@@ -748,7 +932,9 @@ cudaError_t launch_dn(const AttnParams& p, int hb, cudaStream_t stream) {
     case 4:
       if constexpr (NT == 1) return launch_dnh<D, NT, 4>(p, stream);
       break;
-    case 2: return launch_dnh<D, NT, 2>(p, stream);
+    case 2:
+      if constexpr (NT == 1) return launch_dnh<D, NT, 2>(p, stream);
+      break;
     case 1: return launch_dnh<D, NT, 1>(p, stream);
   }
   return cudaErrorInvalidValue;
@@ -757,20 +943,23 @@ cudaError_t launch_dn(const AttnParams& p, int hb, cudaStream_t stream) {
 }  // namespace
 
 // KV heads handled together by one unit: the largest of 4, 2, 1 dividing the
-// KV head count (at most 2 for GQA groups above 8, to fit shared memory).
+// KV head count (1 for GQA groups above 8: a pair then holds at most 16
+// query heads, and the unit-end buffers fit shared memory).
 int attention_heads_per_unit(int q_heads, int kv_heads) {
   const int group = q_heads / kv_heads;
-  const int cap = group <= 8 ? 4 : 2;
+  const int cap = group <= 8 ? 4 : 1;
   for (int hb = cap; hb > 1; hb >>= 1)
     if (kv_heads % hb == 0) return hb;
   return 1;
 }
 
 // Stream-K plan: U = pairs x pair_tiles units cut into one contiguous range
-// per CTA (one CTA per SM, or one per unit when there are fewer).  The
-// workspace holds, per (row, head), slot_group partial slots for each CTA that
-// can meet one pair: the largest such count over the pairs, computed with the
-// same integer arithmetic as the kernels.
+// per CTA (one CTA per SM, or one per unit when there are fewer).  A pair is
+// split where a range boundary falls inside it; when any is, the workspace
+// holds two partial slots per CTA (the first and the last pair its range
+// meets), each [heads of a pair, dim] fp32 plus [heads of a pair] LSE, so
+// its size depends on the CTA count and the pair's heads, not on the rows.
+// The same integer arithmetic as the kernels.
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
                         int use_decode_kernel) {
   (void)use_decode_kernel;
@@ -779,19 +968,29 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
   const int tt = 64 / hb;
   const int64_t pairs = static_cast<int64_t>(rows) * (kv_heads / hb);
   plan.heads_per_unit = hb;
-  plan.slot_group = kGroups * (kGroupWarps / hb);
   plan.pair_tiles = std::max(1, (topk_width + tt - 1) / tt);
   plan.units = pairs * plan.pair_tiles;
-  plan.ctas = static_cast<int>(std::min<int64_t>(plan.units, num_sms()));
+  plan.ctas = static_cast<int>(std::min<int64_t>(plan.units, std::min(num_sms(), kMaxSplit + 1)));
   if (plan.units <= 0) return plan;
   const int64_t U = plan.units, C = plan.ctas, T = plan.pair_tiles;
   auto owner = [&](int64_t x) { return ((x + 1) * C + U - 1) / U - 1; };
-  int64_t most = 1;
-  for (int64_t g = 0; g < pairs; ++g) most = std::max(most, owner(g * T + T - 1) - owner(g * T) + 1);
-  plan.partials = static_cast<int>(most) * plan.slot_group;
-  const size_t o_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * dim * sizeof(float);
-  const size_t l_bytes = static_cast<size_t>(plan.partials) * rows * q_heads * sizeof(float);
-  plan.workspace_bytes = ((o_bytes + 255) & ~static_cast<size_t>(255)) + l_bytes;
+  // most CTAs meeting one split pair: pair of each range's last unit, when
+  // the range holds the pair's first unit and not its last
+  for (int64_t c = 0; c < C; ++c) {
+    const int64_t first = ((U * (c + 1) / C) - 1) / T * T;
+    const int64_t o1 = owner(first), o2 = owner(first + T - 1);
+    if (o1 == c && o2 > c) {
+      plan.merge_pieces = std::max<int>(plan.merge_pieces, static_cast<int>(o2 - c + 1));
+      plan.split_cta[plan.n_split++] = static_cast<int16_t>(c);
+    }
+  }
+  if (plan.merge_pieces == 0) return plan;
+  plan.partials = 2;
+  const size_t hqp = static_cast<size_t>(hb) * (q_heads / kv_heads);
+  const size_t slots = static_cast<size_t>(plan.partials) * plan.ctas;
+  const size_t o_bytes = slots * hqp * dim * sizeof(float);
+  plan.lse_offset = (o_bytes + 255) & ~static_cast<size_t>(255);
+  plan.workspace_bytes = plan.lse_offset + slots * hqp * sizeof(float);
   return plan;
 }
 

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -708,18 +709,20 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.kv_fused = fused ? (k_head_stride == 2 * head_dim ? 2 : 1) : 0;
   p.slot_contig = k_block_stride == static_cast<int64_t>(page_size) * k_token_stride &&
                   k_token_stride == static_cast<int64_t>(num_kv_heads) * k_head_stride;
+  p.gate_vec = gate != nullptr && gate_dim_stride == 1 && aligned(gate, 16) &&
+               gate_row_stride % 8 == 0 && gate_head_stride % 8 == 0;
+  p.out_vec = aligned(out, 16) && out_row_stride % 8 == 0 && out_head_stride % 8 == 0;
   p.pair_tiles = plan.pair_tiles;
   p.sk_ctas = plan.ctas;
   p.sk_units = plan.units;
-  p.slot_group = plan.slot_group;
   p.heads_per_unit = plan.heads_per_unit;
   p.partials = plan.partials;
-  {
-    const size_t o_bytes =
-        static_cast<size_t>(plan.partials) * rows * num_q_heads * head_dim * sizeof(float);
+  p.merge_pieces = plan.merge_pieces;
+  p.n_split = plan.n_split;
+  std::copy(plan.split_cta, plan.split_cta + plan.n_split, p.split_cta);
+  if (plan.partials > 0) {
     p.part_o = static_cast<float*>(workspace);
-    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                          ((o_bytes + 255) & ~static_cast<size_t>(255)));
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.lse_offset);
   }
   p.err = device_error_word();
   cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream));

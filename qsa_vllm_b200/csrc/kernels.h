@@ -103,6 +103,9 @@ struct SelectParams {
 cudaError_t launch_select_decode(const SelectParams& p, cudaStream_t stream, const char** why);
 
 // ------------------------------------------------------------- attention
+// Most pairs a work split can cut: one per boundary between CTA ranges (the
+// planner uses at most kMaxSplit + 1 CTAs).
+constexpr int kMaxSplit = 255;
 struct AttnParams {
   const void* q;
   int64_t q_row_stride, q_head_stride;
@@ -129,27 +132,34 @@ struct AttnParams {
   int physical;
   int kv_fused;     // 2: K||V of consecutive heads contiguous; 1: per head; 0: apart
   int slot_contig;  // consecutive slots are adjacent in memory (block stride = page * token stride)
+  int gate_vec;     // gate rows 16-byte aligned with unit dim stride
+  int out_vec;      // out rows 16-byte aligned
   // Stream-K work split: the (row, kv-head group) pairs x pair_tiles token
   // tiles form sk_units units of work, cut into sk_ctas contiguous ranges
-  // (one per CTA).  A pair's partial results come from the CTAs whose ranges
-  // meet it: slot_group partial slots per CTA (consumer groups x sub-tiles).
+  // (one per CTA).  A pair met by one CTA is finished by it; a pair that a
+  // range boundary splits gets one partial slot from each CTA meeting it.
   int pair_tiles;       // token tiles per pair (upper bound: topk_width / tile)
   int sk_ctas;          // CTAs of the main kernel
   int64_t sk_units;     // pairs * pair_tiles
-  int slot_group;       // partial slots one CTA writes per (row, head) it meets
   int heads_per_unit;   // KV heads per pair
-  int partials;         // partial (O, LSE) slots per (row, head) in the workspace
-  float* part_o;    // [partials, rows, q_heads, dim] fp32
-  float* part_lse;  // [partials, rows, q_heads] fp32
+  int partials;         // partial slots per CTA: 2 when some pair is split, else 0
+  int merge_pieces;     // most CTAs meeting one split pair
+  int n_split;          // split pairs: merge grid columns
+  int16_t split_cta[kMaxSplit];  // per split pair, the CTA holding its first tile
+  float* part_o;    // [partials * sk_ctas, heads of a pair, dim] fp32
+  float* part_lse;  // [partials * sk_ctas, heads of a pair] fp32
   int* err;
 };
 struct AttnPlan {
   int pair_tiles;     // token tiles per (row, kv-head group) pair
   int ctas;           // main-kernel CTAs (contiguous unit ranges)
   int64_t units;      // pairs * pair_tiles
-  int slot_group;     // partial slots per CTA met, per (row, head)
   int heads_per_unit; // KV heads per pair
-  int partials;       // partial slots per (row, head): most CTAs any pair meets * slot_group
+  int partials;       // partial slots per CTA (2 when some pair is split, else 0)
+  int merge_pieces;   // most CTAs meeting one split pair (0: none split)
+  int n_split;        // split pairs
+  int16_t split_cta[kMaxSplit];  // per split pair, the CTA holding its first tile
+  size_t lse_offset;  // byte offset of the LSE slots in the workspace
   size_t workspace_bytes;
 };
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,

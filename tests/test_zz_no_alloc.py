@@ -69,32 +69,40 @@ def test_static_scratch_matches_caller_workspace_on_consecutive_calls():
     assert _lib.device_error_poll() == 0
 
 
-def test_static_scratch_rejects_calls_above_its_maximum():
+def test_static_scratch_need_does_not_grow_with_rows():
+    """The split-K scratch holds two partial slots per CTA, so the need is
+    bounded by the SM count, not the rows: every call fits the static array,
+    and a many-row call through it equals the caller-workspace path."""
+    from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.ensure_device(dev)
     lib = _lib.load_library()
-    rows, hq, hkv, d, width = 1024, 32, 4, 128, 2051
-    need = lib.qsa_sparse_attention_workspace_bytes(rows, hq, hkv, d, width, 1)
-    assert need > (32 << 20)
-    # a call this large is refused on the host before anything is launched or
-    # read: tiny stand-in tensors are enough for the pointers
-    x = torch.zeros(16, dtype=torch.int32, device=dev)
-    n0 = _lib.kernel_launches()
-    status = lib.qsa_sparse_attention_static_scratch(
-        x.data_ptr(), hq * d, d, rows, hq, d,
-        x.data_ptr(), 0, 0, 0, x.data_ptr(), 0, 0, 0, 1, 64, hkv,
-        x.data_ptr(), width, width, x.data_ptr(), 1, 1, 1, x.data_ptr(), x.data_ptr(),
-        None, 0, 0, 0, x.data_ptr(), hq * d, d, 1, 1, torch.cuda.current_stream().cuda_stream)
-    assert status == 3  # QSA_ERR_WORKSPACE
-    assert "static maximum" in lib.qsa_last_error().decode()
-    assert _lib.kernel_launches() == n0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    static_max = 8 << 20
+    for hq, hkv, d in ((32, 4, 128), (16, 2, 128), (16, 1, 128), (64, 4, 64), (8, 8, 128)):
+        bound = 256 + 2 * sms * 32 * (d + 1) * 4
+        for rows in (1, 64, 1024, 8192, 1 << 20):
+            for width, decode in ((2051, 1), (1027, 0), (65539, 1)):
+                need = lib.qsa_sparse_attention_workspace_bytes(rows, hq, hkv, d, width, decode)
+                assert need <= bound <= static_max, (hq, hkv, d, rows, width, need)
+    rows = 3000
+    q, k, v, idx, table, t2r, counts, gate = _case(dev, rows, seed=5)
+    ref = qsa_sparse_paged_attention(q, k, v, idx, table, t2r, output_gate=gate,
+                                     use_decode_kernel=True, indices_are_physical=True,
+                                     valid_counts=counts)
+    out = torch.full_like(q, float("nan"))
+    _lib.check(_static_call(lib, q, k, v, idx, table, t2r, counts, gate, out),
+               "static scratch attention")
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert _lib.device_error_poll() == 0
     assert ctypes.sizeof(ctypes.c_size_t) == 8
 
 
 def test_static_scratch_validates_shapes_before_its_maximum():
-    """A malformed call that would also exceed the static maximum is refused as
-    malformed (invalid / unsupported shape), not as a scratch overflow."""
+    """A malformed call is refused as malformed (invalid / unsupported shape)
+    before any scratch check, and launches nothing."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.ensure_device(dev)
