@@ -300,11 +300,12 @@ __global__ void visible_blocks_kernel(const int64_t* positions, const int32_t* s
                                       int num_requests, const int32_t* token_to_req, int rows,
                                       int ratio, int32_t* visible) {
   // Unlike the other kernels, this one lets its dependents start only after
-  // its counts are written: the next kernel may read them before its own
-  // wait, as step metadata.
+  // its counts are written and made visible device-wide (the fence): the
+  // next kernel may read them before its own wait, as step metadata.
   pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r < rows) visible[r] = visible_of(positions, seq_lens, num_requests, token_to_req, ratio, r);
+  __threadfence();
   pdl_trigger();
 }
 }  // namespace
