@@ -133,8 +133,9 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
   pdl_wait();
   pdl_trigger();
 
-  if (length <= topk) {
-    // Every column is selected (topk.cu:187-191); no score is read.
+  if (length <= topk || topk == 0) {
+    // Every column is selected (topk.cu:187-191), or none is asked for; no
+    // score is read.
     const int n = p.expand ? max(m.complete, 0) : topk;
     for (int j = crank * T + tid; j < n; j += C * T)
       write_rank(p, m, out_row, j, j < length ? j : -1);
@@ -350,6 +351,163 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_kernel(const TopkParams p) {
   if (C > 1) cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
+// Rows of up to kWarpRowKeys keys (prefill rows): ONE WARP per row, the
+// same selection and ordering as topk_kernel with no barrier and no shared
+// histogram.  A lane holds 64 keys in registers (16 coalesced float4 loads:
+// key 4c+e is column 4(32c + lane) + e).  The K-th largest key T is built
+// one bit at a time below the row's common high bits: a bit is kept when at
+// least K keys are >= the candidate (one warp reduction per bit), stopping
+// early once exactly K keys are >= T.  Keys > T are selected, keys == T in
+// column order up to the quota; ids go to the warp's shared-memory buffer by
+// rank, then the expansion writes them out.
+constexpr int kWarpRowKeys = 2048;
+constexpr int kRowWarps = 8;  // rows per CTA
+template <int SELCAP>
+__global__ void __launch_bounds__(kRowWarps * 32, 2) topk_warp_kernel(const TopkParams p) {
+  constexpr int kV = kWarpRowKeys / 32;  // keys per lane
+  constexpr int kChunks = kV / 4;
+  extern __shared__ int smem_w[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* sel = smem_w + warp * SELCAP;
+  const int row = blockIdx.x * kRowWarps + warp;
+  const bool live = row < p.rows;
+  const int topk = p.topk;
+  int32_t* out_row = p.output + static_cast<int64_t>(live ? row : 0) * p.out_row_stride;
+  // row metadata before the wait, as in topk_kernel
+  RowMeta m{};
+  if (live && p.expand) m = row_meta(p, row);
+  const int length =
+      live ? min(max(p.lengths != nullptr ? p.lengths[row]
+                                          : visible_of(p.positions, p.seq_lens, p.num_requests,
+                                                       p.token_to_req, p.ratio, row),
+                     0),
+                 p.width)
+           : 0;
+  pdl_wait();
+  pdl_trigger();
+  if (!live) return;
+
+  if (length <= topk || topk == 0) {  // all columns selected (topk.cu:187-191), or none asked
+    const int n = p.expand ? max(m.complete, 0) : topk;
+    for (int j = lane; j < n; j += 32) write_rank(p, m, out_row, j, j < length ? j : -1);
+    if (p.expand) finish_row<32>(p, m, out_row, row, lane);
+    return;
+  }
+
+  const float* src = p.scores + static_cast<int64_t>(row) * p.score_row_stride;
+  uint32_t key[kV];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int e = 4 * (c * 32 + lane);
+    if (p.vec4 && e + 3 < length) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + e));
+      key[4 * c] = v.x;
+      key[4 * c + 1] = v.y;
+      key[4 * c + 2] = v.z;
+      key[4 * c + 3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        key[4 * c + j] = e + j < length ? __float_as_uint(src[e + j]) : 0u;
+    }
+  }
+  // Slots past the row's length hold key 0 and come last in column order.
+  // They are never >= a candidate (candidates are >= 1) nor > T; as keys
+  // == T (only when T = 0) they follow every valid tie, so the quota never
+  // reaches them, and they are subtracted from the tie count.
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    const bool v = 4 * ((i / 4) * 32 + lane) + (i % 4) < length;
+    kmin = min(kmin, v ? key[i] : 0xffffffffu);
+    kmax = max(kmax, key[i]);
+  }
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  // T starts as the common high bits with zeros below: every valid key is
+  // >= T, so at least K are (length > K).  Each bit below is kept when at
+  // least K keys are >= the candidate; T ends as the K-th largest key.
+  const int common = kmin == kmax ? 32 : __clz(kmin ^ kmax);
+  uint32_t T = common == 0 ? 0u : (kmax >> (32 - common)) << (32 - common);
+  for (int b = 31 - common; b >= 0; --b) {
+    const uint32_t cand = T | (1u << b);
+    int c4[4] = {0, 0, 0, 0};  // independent sums: a short dependency chain
+#pragma unroll
+    for (int i = 0; i < kV; ++i) c4[i & 3] += key[i] >= cand ? 1 : 0;
+    const int c = __reduce_add_sync(0xffffffffu, (c4[0] + c4[1]) + (c4[2] + c4[3]));
+    if (c >= topk) {
+      T = cand;
+      if (c == topk) break;  // exactly K keys >= T: they are the selection
+    }
+  }
+
+  // ---- ordered write-out: keys > T are taken, keys == T in column order up
+  // to the quota.  Per chunk, a warp scan of packed (above << 16 | tied)
+  // counts ranks every key in column order.
+  int above = 0, ties = 0;
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    above += key[i] > T ? 1 : 0;
+    ties += key[i] == T ? 1 : 0;
+  }
+  above = __reduce_add_sync(0xffffffffu, above);
+  ties = __reduce_add_sync(0xffffffffu, ties) - (T == 0u ? kWarpRowKeys - length : 0);
+  const int quota = min(topk - above, ties);
+  int run_strict = 0, run_tie = 0;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    int fs = 0, ft = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      fs += key[4 * c + j] > T;
+      ft += key[4 * c + j] == T;
+    }
+    const int packed = (fs << 16) | ft;
+    int incl = packed;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int ex = incl - packed;
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    int sb = run_strict + (ex >> 16);
+    int tb = run_tie + (ex & 0xffff);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int id = 4 * (c * 32 + lane) + j;
+      if (key[4 * c + j] > T) {
+        sel[sb + min(tb, quota)] = id;
+        ++sb;
+      } else if (key[4 * c + j] == T) {
+        if (tb < quota) sel[sb + tb] = id;
+        ++tb;
+      }
+    }
+    run_strict += tot >> 16;
+    run_tie += tot & 0xffff;
+  }
+  __syncwarp();
+  const int chosen = run_strict + quota;  // = topk
+  for (int i = lane; i < chosen; i += 32) {
+    if (p.expand && i >= m.complete) break;
+    write_rank(p, m, out_row, i, sel[i]);
+  }
+  if (p.expand) finish_row<32>(p, m, out_row, row, lane);
+}
+
+template <int SELCAP>
+cudaError_t launch_warp_rows(const TopkParams& p, cudaStream_t stream) {
+  const int smem = kRowWarps * SELCAP * static_cast<int>(sizeof(int));
+  cudaError_t e = set_attr_once(reinterpret_cast<const void*>(topk_warp_kernel<SELCAP>),
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const unsigned blocks = static_cast<unsigned>((p.rows + kRowWarps - 1) / kRowWarps);
+  return count_launches(launch_kernel(topk_warp_kernel<SELCAP>, dim3(blocks),
+                                      dim3(kRowWarps * 32), static_cast<size_t>(smem), stream,
+                                      1, p));
+}
+
 int pow2_ceil(int x) {
   int c = 1;
   while (c < x) c <<= 1;
@@ -383,6 +541,14 @@ cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_clu
   if (p.rows <= 0) return cudaSuccess;
   // Rows of one CTA at 8 keys per thread: the narrowest CTA that covers them.
   const int w = std::max(p.width, 1);
+  // One warp per row has a longer per-row latency than a 256-thread CTA but
+  // runs four times as many rows per SM: it pays off from about three waves
+  // of the CTA form (4 CTAs per SM) on.
+  if (w <= kWarpRowKeys && p.topk <= 1024 && p.rows >= 12 * num_sms()) {
+    p.slice_cap = kWarpRowKeys;
+    if (plan_cluster) *plan_cluster = 1;
+    return p.topk <= 256 ? launch_warp_rows<256>(p, stream) : launch_warp_rows<1024>(p, stream);
+  }
   if (w <= 256 * 8) {
     p.slice_cap = 256 * 8;
     if (plan_cluster) *plan_cluster = 1;

@@ -94,19 +94,23 @@ __device__ __forceinline__ void write_rank(const TopkParams& p, const RowMeta& m
   store_block(p, m, out_row, rank, block, ph);
 }
 
-// Causal tail, -1 fill and valid count (topk.cu:152-162).  T threads.
+// Causal tail, -1 fill and valid count (topk.cu:152-162), by threads
+// tid = 0..T-1 of a group.
 template <int T>
 __device__ __forceinline__ void finish_row(const TopkParams& p, const RowMeta& m,
-                                           int32_t* out_row, int row) {
+                                           int32_t* out_row, int row, int tid) {
   const int expanded = m.complete * p.ratio;
-  for (int col = max(expanded, 0) + static_cast<int>(threadIdx.x); col < p.out_width;
-       col += T) {
+  for (int col = max(expanded, 0) + tid; col < p.out_width; col += T) {
     const int off = col - expanded;
     out_row[static_cast<int64_t>(col) * p.out_col_stride] =
         (off < m.tail_count && off < p.ratio - 1) ? map_token(p, m, m.tail_start + off) : -1;
   }
-  if (p.counts != nullptr && threadIdx.x == 0)
-    p.counts[row] = min(expanded + m.tail_count, m.seq);
+  if (p.counts != nullptr && tid == 0) p.counts[row] = min(expanded + m.tail_count, m.seq);
+}
+template <int T>
+__device__ __forceinline__ void finish_row(const TopkParams& p, const RowMeta& m,
+                                           int32_t* out_row, int row) {
+  finish_row<T>(p, m, out_row, row, static_cast<int>(threadIdx.x));
 }
 
 // Block-wide (W warps) exclusive prefix sum of one int per thread; also

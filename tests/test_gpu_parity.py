@@ -103,6 +103,23 @@ def test_topk_expand_cluster_widths(dev, rows, width, topk):
         assert np.array_equal(counts, ref_counts)
 
 
+@pytest.mark.parametrize("rows,width,token_topk", [(1779, 2048, 1024), (1803, 2000, 1200),
+                                                   (1801, 2048, 4096), (1790, 1500, 4400),
+                                                   (1777, 700, 0), (33, 2048, 1024),
+                                                   (12, 700, 0)])
+def test_topk_expand_warp_rows(dev, rows, width, token_topk):
+    """Many rows of <= 2048 keys (>= 12 per SM) run one warp per row: row
+    counts that do not fill the CTA's 8 warps, both selection buffer sizes
+    (top-k <= 256, <= 1024), the block kernel above top-k 1024 and for few
+    rows, and top-k 0 (only the causal tail)."""
+    for i, kind in enumerate(("relu", "ties", "signed", "zeros")):
+        case = make_case(rows * 13 + width + i, rows, width, token_topk, kind=kind)
+        got, counts = run_topk_expand(case, dev)
+        ref, ref_counts = oracle_topk_expand(case)
+        assert np.array_equal(got, ref), (kind, np.argwhere(got != ref)[:5])
+        assert np.array_equal(counts, ref_counts), kind
+
+
 def test_topk_plain_matches_oracle(dev):
     from qsa_vllm_b200.topk import topk
     for seed, (rows, width, k) in enumerate([(5, 100, 16), (4, 9000, 512), (2, 40000, 2048)]):
