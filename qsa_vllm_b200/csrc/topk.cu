@@ -442,8 +442,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 2) topk_warp_kernel(const Topk
   }
 
   // ---- ordered write-out: keys > T are taken, keys == T in column order up
-  // to the quota.  Per chunk, a warp scan of packed (above << 16 | tied)
-  // counts ranks every key in column order.
+  // to the quota.
   int above = 0, ties = 0;
 #pragma unroll
   for (int i = 0; i < kV; ++i) {
@@ -453,42 +452,71 @@ __global__ void __launch_bounds__(kRowWarps * 32, 2) topk_warp_kernel(const Topk
   above = __reduce_add_sync(0xffffffffu, above);
   ties = __reduce_add_sync(0xffffffffu, ties) - (T == 0u ? kWarpRowKeys - length : 0);
   const int quota = min(topk - above, ties);
-  int run_strict = 0, run_tie = 0;
+  const unsigned lt = (1u << lane) - 1u;  // lanes below this one
+  int run = 0;
+  if (quota == ties) {
+    // every valid key >= T is taken (invalid slots, key 0, only when T > 0):
+    // a key's rank is the number of taken keys before it in column order
+    // (chunk, lane, j), from one ballot per (chunk, j)
+    const bool t0 = T != 0u;
 #pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    int fs = 0, ft = 0;
+    for (int c = 0; c < kChunks; ++c) {
+      bool tk[4];
+      unsigned mk[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      fs += key[4 * c + j] > T;
-      ft += key[4 * c + j] == T;
+      for (int j = 0; j < 4; ++j) {
+        tk[j] = key[4 * c + j] > T || (key[4 * c + j] == T && (t0 || 4 * (c * 32 + lane) + j < length));
+        mk[j] = __ballot_sync(0xffffffffu, tk[j]);
+      }
+      int r = run;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r += __popc(mk[j] & lt);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (tk[j]) sel[r] = 4 * (c * 32 + lane) + j;
+        r += tk[j] ? 1 : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) run += __popc(mk[j]);
     }
-    const int packed = (fs << 16) | ft;
-    int incl = packed;
+  } else {
+    // ties straddle the threshold: the first `quota` of them in column order
+    int run_tie = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    const int ex = incl - packed;
-    const int tot = __shfl_sync(0xffffffffu, incl, 31);
-    int sb = run_strict + (ex >> 16);
-    int tb = run_tie + (ex & 0xffff);
+    for (int c = 0; c < kChunks; ++c) {
+      unsigned ms[4], mt[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int id = 4 * (c * 32 + lane) + j;
-      if (key[4 * c + j] > T) {
-        sel[sb + min(tb, quota)] = id;
-        ++sb;
-      } else if (key[4 * c + j] == T) {
-        if (tb < quota) sel[sb + tb] = id;
-        ++tb;
+      for (int j = 0; j < 4; ++j) {
+        ms[j] = __ballot_sync(0xffffffffu, key[4 * c + j] > T);
+        mt[j] = __ballot_sync(0xffffffffu, key[4 * c + j] == T);
+      }
+      int sb = run, tb = run_tie;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sb += __popc(ms[j] & lt);
+        tb += __popc(mt[j] & lt);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int id = 4 * (c * 32 + lane) + j;
+        if (key[4 * c + j] > T) {
+          sel[sb + min(tb, quota)] = id;
+          ++sb;
+        } else if (key[4 * c + j] == T) {
+          if (tb < quota) sel[sb + tb] = id;
+          ++tb;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        run += __popc(ms[j]);
+        run_tie += __popc(mt[j]);
       }
     }
-    run_strict += tot >> 16;
-    run_tie += tot & 0xffff;
+    run += quota;
   }
   __syncwarp();
-  const int chosen = run_strict + quota;  // = topk
+  const int chosen = run;  // = topk
   for (int i = lane; i < chosen; i += 32) {
     if (p.expand && i >= m.complete) break;
     write_rank(p, m, out_row, i, sel[i]);
