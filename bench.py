@@ -175,42 +175,51 @@ class ClockSampler:
                 "source": "NVML, every 2 ms during the timed region"}
 
 
+def oracle_sample(cfg: str, rows: int):
+    """A CPU workload with ``rows`` rows of ``cfg``'s per-row shapes and the
+    oracle step that runs it: decode rows are ``rows`` requests; prefill rows
+    are the last ``rows`` new tokens of one request (same context and causal
+    visibility as the configuration's chunk ends)."""
+    from oracle import qsa_oracle as O
+    from qsa_vllm_b200.synthetic import CONFIGS, make_workload
+    if CONFIGS[cfg].get("new_tokens") is None:
+        return make_workload(cfg, device="cpu", seed=0, batch=rows), O.decode_step, "decode_step"
+    w = make_workload(cfg, device="cpu", seed=0, batch=1, new_tokens=rows)
+    return w, O.prefill_step, "prefill_step"
+
+
 def cpu_baseline(cfg: str, rows: int = 4, min_seconds: float = 10.0) -> dict:
     """The CPU oracle on a bounded sample: ``rows`` rows of the same workload."""
-    from oracle import qsa_oracle as O
-    from qsa_vllm_b200.synthetic import make_workload
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    w = make_workload(cfg, device="cpu", seed=0, batch=rows)
-    O.decode_step(w)
+    w, step, name = oracle_sample(cfg, rows)
+    step(w)
     n, t0 = 0, time.perf_counter()
     while True:
-        O.decode_step(w)
+        step(w)
         n += 1
         el = time.perf_counter() - t0
         if el >= min_seconds or n >= 5000:
             break
     return {"value": rows * n / el, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{rows} of the workload's rows ({cfg} per-row shapes) x {n} passes "
-                      f"of oracle.decode_step, {el:.1f} s"}
+                      f"of oracle.{name}, {el:.1f} s"}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import qsa_oracle as O
-    from qsa_vllm_b200.synthetic import make_workload
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     rows = args.ref_rows
-    w = make_workload(args.config, device="cpu", seed=0, batch=rows)
+    w, step, name = oracle_sample(args.config, rows)
     for _ in range(args.warmup):
-        O.decode_step(w)
+        step(w)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.decode_step(w)
+        step(w)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = rows * args.steps / total

@@ -458,6 +458,27 @@ def decode_step(w, *, round_p: bool = True):
     return out, idx, counts, logits
 
 
+def prefill_step(w, *, round_p: bool = True):
+    """One QSA chunked-prefill step on CPU tensors of a ``SyntheticQSA``
+    workload ``w``: scores over each row's causal visible blocks
+    (ops/indexer.py:282-343, logits width as :262-263), top-k expanded to
+    logical token ids (no block table), attention through the request's block
+    table (ops/qsa.py:594-688 with use_decode_kernel=False).
+
+    Returns (attention_out fp32 [rows, H_q, d], topk_indices, counts, logits).
+    """
+    vis = visible_blocks(w.positions, w.seq_lens, w.token_to_req, w.ratio)
+    columns = -(-(-(-int(w.max_seq_len) // w.ratio)) // 64) * 64
+    logits = indexer_scores(w.index_q, w.index_cache, w.index_table, vis, columns,
+                            query_start_loc=w.query_start_loc, weights=w.index_weights,
+                            scale=w.index_scale)
+    idx, counts = topk_expand(logits, vis, w.positions, w.seq_lens, w.token_to_req, None,
+                              w.token_topk + w.ratio - 1, w.ratio)
+    out = sparse_attention(w.q, w.k_cache, w.v_cache, torch.from_numpy(idx), w.block_table,
+                           w.token_to_req, output_gate=w.gate, round_p=round_p)
+    return out, idx, counts, logits
+
+
 def _bf16_trunc(x: torch.Tensor) -> torch.Tensor:
     """fp32 -> bf16 rounding toward zero (low 16 bits cleared), returned as fp32."""
     return (x.float().contiguous().view(torch.int32) & -65536).view(torch.float32)

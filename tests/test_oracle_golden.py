@@ -168,3 +168,23 @@ def test_prepare_oracle_matches_reference_interpreter(name):
     assert torch.equal(q, torch.from_numpy(d[f"{name}_out_index_q"]))
     for k, v in caches.items():
         assert torch.equal(v, torch.from_numpy(d[f"{name}_out_{k}"])), k
+
+
+def test_prefill_step_composes_the_pinned_pieces():
+    """oracle.prefill_step (the prefill CPU baseline of bench.py) is the pinned
+    indexer, top-k and attention functions chained: logical ids inside each
+    row's causal window, counts as the expansion rules give them."""
+    from qsa_vllm_b200.synthetic import make_workload
+    w = make_workload("cfg1", device="cpu", seed=0, batch=1, new_tokens=3, seq_len=2048)
+    out, idx, counts, logits = O.prefill_step(w)
+    assert out.shape == w.q.shape and idx.shape == (3, w.token_topk + w.ratio - 1)
+    pos, seq, rr = w.positions.numpy(), int(w.seq_lens[0]), w.ratio
+    for r in range(3):
+        valid = idx[r][idx[r] >= 0]
+        complete = min((pos[r] + 1) // rr, seq // rr, w.token_topk // rr)
+        assert valid.size == counts[r] == min(complete * rr + (pos[r] + 1) % rr, seq)
+        assert valid.max() <= pos[r] and len(set(valid.tolist())) == valid.size
+    vis = O.visible_blocks(w.positions, w.seq_lens, w.token_to_req, w.ratio)
+    ref, _ = O.topk_expand(logits, vis, w.positions, w.seq_lens, w.token_to_req, None,
+                           w.token_topk + w.ratio - 1, w.ratio)
+    assert np.array_equal(idx, ref)
