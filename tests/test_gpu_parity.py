@@ -373,6 +373,38 @@ def test_attention_matches_oracle(dev, rows, hq, hkv, d, physical, gate, counts)
     _attention_check(out, ref)
 
 
+@pytest.mark.parametrize("rows,hq,hkv,d,physical", [(300, 16, 2, 128, False), (5, 16, 2, 128, True),
+                                                   (200, 8, 2, 64, False), (40, 32, 2, 128, False)])
+def test_attention_strided_gate_and_output(dev, rows, hq, hkv, d, physical):
+    """Gate with a non-unit dim stride and output rows that are only 4-byte
+    aligned: the scalar gate loads and 4-byte output stores, on pairs finished
+    in the main kernel (many rows) and on split pairs (few rows)."""
+    from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
+    g = torch.Generator().manual_seed(rows + d)
+    page, nblk = 16, 64
+    width = 259
+    kv = torch.randn(nblk, page, hkv, 2 * d, generator=g).to(torch.bfloat16)
+    q = (torch.randn(rows, hq, d, generator=g) * d ** -0.5 * 4).to(torch.bfloat16)
+    table = torch.randperm(nblk, generator=g)[:nblk // 2].view(2, nblk // 4).to(torch.int32)
+    t2r = torch.randint(0, 2, (rows,), generator=g).to(torch.int32)
+    hi = nblk * page if physical else (nblk // 4) * page
+    idx = torch.randint(-1, hi, (rows, width), generator=g).to(torch.int32)
+    gate_t = torch.randn(rows, d, hq, generator=g).to(torch.bfloat16)
+    gate = gate_t.to(dev).permute(0, 2, 1)            # dim stride hq
+    assert gate.stride(2) != 1
+    buf = torch.full((rows, hq, d + 2), float("nan"), dtype=torch.bfloat16, device=dev)
+    out = buf[:, :, 2:]                                # rows start 4 bytes past 16-byte alignment
+    qsa_sparse_paged_attention(q.to(dev), kv.to(dev)[..., :d], kv.to(dev)[..., d:], idx.to(dev),
+                               table.to(dev), t2r.to(dev), out, output_gate=gate,
+                               use_decode_kernel=physical, indices_are_physical=physical)
+    torch.cuda.synchronize()
+    ref = O.sparse_attention(q, kv[..., :d], kv[..., d:], idx, table, t2r,
+                             output_gate=gate_t.permute(0, 2, 1), use_decode_kernel=physical,
+                             indices_are_physical=physical)
+    _attention_check(out, ref)
+    assert torch.isnan(buf[:, :, :2].float()).all()   # nothing written outside the view
+
+
 def test_attention_separate_kv_buffers(dev):
     """K and V in different allocations (two bulk copies per token)."""
     from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
