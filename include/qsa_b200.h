@@ -75,6 +75,14 @@ QSA_API int qsa_device_check(void);
  * QSA_DEVICE_ERR_* recorded by kernels whose bounded waits expired.
  */
 QSA_API int qsa_device_error_poll(int32_t* error_bits);
+/*
+ * Self-test of the bounded-wait error path, no counterpart in the reference:
+ * launches one CTA that waits on a barrier phase nothing completes.  The wait
+ * gives up after its 1 s limit and sets QSA_DEVICE_ERR_WAIT_TIMEOUT in the
+ * device error word (read it with qsa_device_error_poll); the kernel returns
+ * normally and the context stays usable.  Takes about one second of GPU time.
+ */
+QSA_API int qsa_selftest_wait_timeout(void* stream);
 enum {
   QSA_DEVICE_ERR_WAIT_TIMEOUT = 1, /* a bounded wait expired */
   QSA_DEVICE_ERR_OUT_OF_RANGE = 2  /* a slot / position / request outside its buffer was skipped */

@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple] = {
     "qsa_set_attention_timing_events": (C.c_int, [_vp, _vp]),
     "qsa_device_check": (C.c_int, []),
     "qsa_device_error_poll": (C.c_int, [C.POINTER(_i32)]),
+    "qsa_selftest_wait_timeout": (C.c_int, [C.c_void_p]),
     "qsa_topk_expand": (C.c_int, [
         _vp, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i32,
         _vp, _i64, _i64, _i32, _vp, _i32, _i32, _i32, _vp]),

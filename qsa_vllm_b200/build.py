@@ -24,7 +24,7 @@ CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "libqsa_b200.so"
 SOURCES = ["capi.cu", "topk.cu", "indexer.cu", "indexer_tc.cu", "select_decode.cu", "attention.cu",
-           "static_scratch.cu", "prepare.cu"]
+           "static_scratch.cu", "prepare.cu", "selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
          "-fvisibility=hidden", "--expt-relaxed-constexpr", f"-I{ROOT / 'include'}"]

@@ -181,6 +181,14 @@ int qsa_device_error_poll(int32_t* error_bits) {
   return QSA_OK;
 }
 
+int qsa_selftest_wait_timeout(void* stream) {
+  int* w = device_error_word();
+  if (w == nullptr) return fail(QSA_ERR_CUDA, "device error word unavailable");
+  cudaError_t e = launch_wait_timeout_selftest(w, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "qsa_selftest_wait_timeout");
+  return QSA_OK;
+}
+
 // ------------------------------------------------------------------ top-k
 static int topk_common(TopkParams& p, void* stream, const char* who) {
   if (p.rows < 0 || p.width < 0) return fail(QSA_ERR_INVALID, "%s: negative rows/width", who);

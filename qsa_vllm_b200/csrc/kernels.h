@@ -214,6 +214,9 @@ struct PrepareParams {
 cudaError_t launch_prepare(const PrepareParams& p, cudaStream_t stream);
 
 int num_sms();
+// One CTA waits on an mbarrier phase nothing completes; the bounded wait
+// expires and records kDeviceErrWaitTimeout in *err (selftest.cu).
+cudaError_t launch_wait_timeout_selftest(int* err, cudaStream_t stream);
 // Records this host thread's attention timing event `which` (0: before the
 // main attention kernel, 1: after it) on `stream`, when one is set.
 void record_attention_event(int which, cudaStream_t stream);

@@ -604,3 +604,24 @@ def test_visible_blocks_kernel_matches_reference_formula(dev):
     for ratio in (1, 4, 7):
         got = compute_visible_blocks(pos.to(dev), seq.to(dev), t2r.to(dev), ratio).cpu()
         assert torch.equal(got, O.visible_blocks(pos, seq, t2r, ratio))
+
+
+def test_bounded_wait_expires_reports_and_leaves_the_context_usable(dev):
+    """The error path shared by every kernel's bounded waits: a wait on a
+    barrier phase that nothing completes gives up after its 1 s limit, sets
+    QSA_DEVICE_ERR_WAIT_TIMEOUT in the device error word, and the next calls
+    run normally with no error recorded."""
+    from qsa_vllm_b200 import _lib
+    from qsa_vllm_b200.topk import topk
+    lib = _lib.load_library()
+    assert _lib.device_error_poll() == 0
+    _lib.check(lib.qsa_selftest_wait_timeout(_lib.stream_ptr(dev)), "wait-timeout self-test")
+    torch.cuda.synchronize()
+    assert _lib.device_error_poll() == 1      # QSA_DEVICE_ERR_WAIT_TIMEOUT
+    assert _lib.device_error_poll() == 0      # read-and-clear
+    case = make_case(91, 3, 500, 64, kind="relu")
+    out = torch.full((3, 64), -7, dtype=torch.int32, device=dev)
+    topk(case["scores"].to(dev), case["lengths"].to(dev), out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.topk_plain(case["scores"], case["lengths"], 64))
+    assert _lib.device_error_poll() == 0
