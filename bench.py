@@ -389,10 +389,11 @@ def main() -> None:
     # ---- end to end through the public API with host buffers
     # The step's inputs live in persistent device buffers (typed views,
     # 256-byte aligned) mirrored by pinned host buffers, as vLLM stages its
-    # per-step inputs.  Two staging groups: the indexer's inputs (metadata,
-    # index queries) are copied before the step; the attention-only inputs
-    # (q, gate) are copied on a second stream while the indexer and top-k run,
-    # and attention waits for them.  One device->host copy of the output.
+    # per-step inputs.  Two staging groups copied concurrently at the step's
+    # start: the indexer's inputs (metadata, index queries) on the main
+    # stream, the attention-only inputs (q, gate) on a second stream while the
+    # indexer and top-k run; attention waits for them.  One device->host copy
+    # of the output.
     def stage(names):
         names = [n for n in names if getattr(w, n) is not None]
         offs, total = [], 0
@@ -418,20 +419,21 @@ def main() -> None:
     h2d = dev_meta.numel() + dev_qg.numel()
     d2h = host_out.numel() * host_out.element_size()
     side = torch.cuda.Stream(dev)
-    meta_ready = torch.cuda.Event()
+    step_start = torch.cuda.Event()
     qg_ready = torch.cuda.Event()
 
     def e2e_step():
         main = torch.cuda.current_stream(dev)
-        dev_meta.copy_(host_meta, non_blocking=True)
-        # one host->device copy at a time: the indexer's inputs first, then q
-        # and gate (after the previous step's attention, which meta_ready also
-        # orders), overlapped with the indexer and top-k
-        meta_ready.record(main)
-        side.wait_event(meta_ready)
+        # both host->device copies start at once, on two streams: the
+        # indexer's inputs on the main stream, q and gate on the side stream
+        # (after the previous step's attention, which step_start orders),
+        # overlapped with the indexer and top-k
+        step_start.record(main)
+        side.wait_event(step_start)
         with torch.cuda.stream(side):
             dev_qg.copy_(host_qg, non_blocking=True)
             qg_ready.record(side)
+        dev_meta.copy_(host_meta, non_blocking=True)
         select_paged_tokens(
             w.index_q, w.index_cache, w.index_table, w.token_to_req, w.positions, w.seq_lens,
             w.token_topk, w.ratio, idx_buf, **w.select_kwargs(),
@@ -505,8 +507,9 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
                 "api": "select_paged_tokens + qsa_sparse_paged_attention with the step's "
-                       "pinned-host -> device input copies (indexer inputs first; q and "
-                       "gate on a second stream, overlapped with the indexer and top-k) and "
+                       "pinned-host -> device input copies (indexer inputs on the main "
+                       "stream and q and gate on a second stream, both from the step's "
+                       "start, overlapped with the indexer and top-k) and "
                        "the device -> host output copy, captured in one CUDA graph as vLLM "
                        "runs decode",
                 "eager_ms_per_step": ms_e2e_eager},
