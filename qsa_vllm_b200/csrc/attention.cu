@@ -31,9 +31,7 @@
 //    accumulator chains; P^T is transposed in registers (movmatrix) into the
 //    B operand of O^T = V^T.P^T.
 //  * At the end of a pair the softmax states of the warps that share a KV
-//    head are folded together in shared memory (deferred: the group that
-//    took the pair's last tile deposits and moves on, the other group folds
-//    and stores, hand-off through bounded mbarrier waits).  A pair met by one CTA only
+//    head are folded together in shared memory.  A pair met by one CTA only
 //    (the common case at prefill) is finished there: normalised, rounded to
 //    bf16, gated and stored.  A range boundary inside a pair splits it:
 //    each piece writes a normalised fp32 partial + LSE (the reference's
