@@ -84,7 +84,6 @@ struct Smem {
   // [head][dim] fp32 result (at most 32 heads)
   alignas(16) float comb[32 * D];
   float cm[4][8], cl[4][8];  // writer slot: m and l of its 8 head columns
-  uint64_t dfull[HB], rfree[HB];  // deferred fold: per KV head, deposits in / region free
   uint64_t mask[kStages];
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -468,36 +467,30 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   bool aborted = false;
   int it = 0, k = 0;
   const int hqp = HB * group;  // query heads of a pair
-  // The R = 8 / HB warps sharing KV head hh: SUB in each consumer group.
-  // With one n8 column block per warp (NT == 1) the unit-end fold is
-  // deferred: the group that takes the unit's last tile (and so finishes
-  // last) deposits its state and moves on; the other group folds and stores.
+  // The R = 8 / HB warps sharing KV head hh.
   constexpr int R = kGroups * SUB;
-  constexpr bool kDefer = NT == 1;
-  constexpr int kOutThreads = kDefer ? SUB * 32 : R * 32;  // threads storing a pair's result
-  constexpr int kItems = (8 * NT * (D / 8) + kOutThreads - 1) / kOutThreads;
+  constexpr int kItems = kOutItems<D, HB, NT>;
   const int head0 = hh * group;  // first query head of hh within the pair
   for (; k < units; ++k) {
     const Unit x = unit_of<TT>(p, groups, ua, ub, k);
     const int qb = k & 1;
-    // late: this warp's group takes the unit's last tile.  Synchronous fold
-    // (NT == 2): rank j among the head's R warps, the late group above, so in
-    // the first round it only stores its state.  tr: rank among the threads
-    // that store the result.
+    // Rank j of this warp among the head's R warps for the unit-end fold:
+    // the group that takes the unit's last tile (and so finishes last) ranks
+    // above the other, so in the first folding round it only stores its
+    // state and the warps that finished earlier do the folding.  tr: thread
+    // rank.
     const int lastg = (it + max(x.t1 - x.t0, 1) - 1) % kGroups;
-    const bool late = cg == lastg;
-    const int j = (late ? SUB : 0) + sub;
-    const int tr = kDefer ? sub * 32 + lane : j * 32 + lane;
-    const bool stores = !kDefer || !late;
+    const int j = (cg == lastg ? SUB : 0) + sub;
+    const int tr = j * 32 + lane;
     // The gate chunks this thread stores at the unit's end, loaded now so
     // their latency hides behind the unit's tiles.
     uint4 gpre[kItems];
 #pragma unroll
     for (int i = 0; i < kItems; ++i) gpre[i] = make_uint4(0, 0, 0, 0);
-    if (p.gate != nullptr && x.pieces == 1 && stores) {
+    if (p.gate != nullptr && x.pieces == 1) {
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
-        const int item = tr + i * kOutThreads;
+        const int item = tr + i * R * 32;
         if (item < group * (D / 8))
           gpre[i] = load_gate8(p, x.row, x.hg * hqp + head0 + item / (D / 8),
                                (item % (D / 8)) * 8);
@@ -613,8 +606,17 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
     }
 
+    // ---- unit end: fold the softmax states of the R warps sharing a KV
+    // head by halving.  Each head has its own shared-memory region (32 D / HB
+    // floats: R / 2 exchange slots of (D / 16) float4 per lane, later its
+    // GQA group's [head][dim] result) and its own named barrier, so heads do
+    // not wait for each other.  Round 1: warp j >= R/2 stores its (O, m, l)
+    // in slot j - R/2 and warp j - R/2 folds it in; later rounds: warp j in
+    // [half, 2 half) stores in its own slot j, the one it read last round
+    // (no one else reads it), and warp j - half folds it in.  All warps of
+    // a head meet every barrier (aborted warps fold in an empty state).
     aborted = __any_sync(0xffffffffu, aborted);
-    if (aborted) {  // aborted warps fold in an empty state (l = 0, O = 0)
+    if (aborted) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         l[nt][0] = l[nt][1] = 0.f;
@@ -631,166 +633,106 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 8);
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 16);
       }
-    // Each KV head has its own shared-memory region (32 D / HB floats):
-    // exchange slots of (D / 16) float4 per lane (one column block), later
-    // the head's GQA group of results as [q head][dim] fp32.
     float* region = sm.comb + hh * (32 * D / HB);
     float4* slots4 = reinterpret_cast<float4*>(region);
-    // store this warp's (O, m, l) of column block nt in exchange slot `slot`
-    auto put = [&](int nt, int slot) {
-      const int cs = hh * (R / 2) + slot;  // the pair's m/l slot
+    const int bar_id = 1 + hh, bar_n = R * 32;
 #pragma unroll
-      for (int mt = 0; mt < KS; ++mt)
-        slots4[(slot * KS + mt) * 32 + lane] =
-            make_float4(o[mt][nt][0], o[mt][nt][1], o[mt][nt][2], o[mt][nt][3]);
-      if (g == 0) {
+    for (int nt = 0; nt < NT; ++nt) {
+      // region free: the head's warps are done with its previous contents
+      named_barrier(bar_id, bar_n);
 #pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {
-          sm.cm[cs][2 * t4 + hc] = m[nt][hc];
-          sm.cl[cs][2 * t4 + hc] = l[nt][hc];
+      for (int half = R / 2; half >= 1; half >>= 1) {
+        if (j >= half && j < 2 * half) {
+          const int slot = half == R / 2 ? j - half : j;
+          const int cs = hh * (R / 2) + slot;  // the pair's m/l slot
+          __syncwarp();
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt)
+            slots4[(slot * KS + mt) * 32 + lane] =
+                make_float4(o[mt][nt][0], o[mt][nt][1], o[mt][nt][2], o[mt][nt][3]);
+          if (g == 0) {
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              sm.cm[cs][2 * t4 + hc] = m[nt][hc];
+              sm.cl[cs][2 * t4 + hc] = l[nt][hc];
+            }
+          }
         }
-      }
-    };
-    // fold the state stored in exchange slot `slot` into this warp's
-    auto fold = [&](int nt, int slot) {
-      const int cs = hh * (R / 2) + slot;
-      float sa[2], sb[2];
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        const float m2 = sm.cm[cs][2 * t4 + hc];
-        const float mx = fmaxf(m[nt][hc], m2);
-        sa[hc] = fast_exp2(m[nt][hc] - mx);
-        sb[hc] = fast_exp2(m2 - mx);
-        l[nt][hc] = l[nt][hc] * sa[hc] + sm.cl[cs][2 * t4 + hc] * sb[hc];
-        m[nt][hc] = mx;
-      }
-#pragma unroll
-      for (int mt = 0; mt < KS; ++mt) {
-        const float4 t = slots4[(slot * KS + mt) * 32 + lane];
-        o[mt][nt][0] = o[mt][nt][0] * sa[0] + t.x * sb[0];
-        o[mt][nt][1] = o[mt][nt][1] * sa[1] + t.y * sb[1];
-        o[mt][nt][2] = o[mt][nt][2] * sa[0] + t.z * sb[0];
-        o[mt][nt][3] = o[mt][nt][3] * sa[1] + t.w * sb[1];
-      }
-    };
-    // ---- the head's result, staged by the warp holding the folded state
-    // (`leader`) as [q head][dim] fp32 (8-float chunks XOR-swizzled by head:
-    // conflict-free fragment stores, 16-byte reads), then stored by the
-    // kOutThreads threads of rank tr (`sync` orders the staging before their
-    // reads).  A pair this CTA met whole is stored as bf16 output with the
-    // gate (ops/qsa.py:250-275); a piece of a split pair as a normalised fp32
-    // partial and its base-2 LSE in slot 2 * cta + (first pair met ? 0 : 1).
-    const bool whole = x.pieces == 1;
-    const int pslot = 2 * static_cast<int>(blockIdx.x) + (k == 0 ? 0 : 1);
-    auto finish_pair = [&](bool leader, auto&& sync) {
-      if (leader) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
+        named_barrier(bar_id, bar_n);
+        if (j < half) {
+          const int slot = half == R / 2 ? j : j + half;
+          const int cs = hh * (R / 2) + slot;
+          float sa[2], sb[2];
 #pragma unroll
           for (int hc = 0; hc < 2; ++hc) {
-            const int hl = 8 * nt + 2 * t4 + hc;
-            if (hl >= group) continue;
-            const float lv = l[nt][hc];
-            const float inv = lv > 0.f ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
-            float* srow = region + hl * D;
-            const int sw = (hl >> 1) & 3;
+            const float m2 = sm.cm[cs][2 * t4 + hc];
+            const float mx = fmaxf(m[nt][hc], m2);
+            sa[hc] = fast_exp2(m[nt][hc] - mx);
+            sb[hc] = fast_exp2(m2 - mx);
+            l[nt][hc] = l[nt][hc] * sa[hc] + sm.cl[cs][2 * t4 + hc] * sb[hc];
+            m[nt][hc] = mx;
+          }
 #pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-              srow[(((2 * mt) ^ sw) << 3) + g] = o[mt][nt][hc] * inv;
-              srow[(((2 * mt + 1) ^ sw) << 3) + g] = o[mt][nt][2 + hc] * inv;
-            }
-            if (!whole && g == 0)
-              p.part_lse[static_cast<int64_t>(pslot) * hqp + head0 + hl] =
-                  lv > 0.f ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
+          for (int mt = 0; mt < KS; ++mt) {
+            const float4 t = slots4[(slot * KS + mt) * 32 + lane];
+            o[mt][nt][0] = o[mt][nt][0] * sa[0] + t.x * sb[0];
+            o[mt][nt][1] = o[mt][nt][1] * sa[1] + t.y * sb[1];
+            o[mt][nt][2] = o[mt][nt][2] * sa[0] + t.z * sb[0];
+            o[mt][nt][3] = o[mt][nt][3] * sa[1] + t.w * sb[1];
           }
         }
       }
-      sync();
-      if (whole) {
-#pragma unroll
-        for (int i = 0; i < kItems; ++i) {
-          const int item = tr + i * kOutThreads;
-          if (item >= group * (D / 8)) continue;
-          const int hl = item / (D / 8), c = item % (D / 8);
-          const float4* src =
-              reinterpret_cast<const float4*>(region + hl * D + ((c ^ ((hl >> 1) & 3)) << 3));
-          store_out8(p, x.row, x.hg * hqp + head0 + hl, c * 8, src[0], src[1], gpre[i]);
-        }
-      } else {
-        float4* po = reinterpret_cast<float4*>(p.part_o +
-                                               (static_cast<int64_t>(pslot) * hqp + head0) * D);
-        for (int item = tr; item < group * (D / 4); item += kOutThreads) {
-          const int hl = item / (D / 4), c4 = item % (D / 4);
-          po[item] = *reinterpret_cast<const float4*>(
-              region + hl * D + (((c4 >> 1) ^ ((hl >> 1) & 3)) << 3) + (c4 & 1) * 4);
-        }
-      }
-    };
-
-    if constexpr (kDefer) {
-      // ---- deferred fold (one column block).  The late group's warps store
-      // their states in slots 0..SUB-1 of the head's region and go on at
-      // once (mbarrier dfull); the other group's warp `sub` folds slot `sub`
-      // in, then those SUB warps fold among themselves by halving (warp sub
-      // in [half, 2 half) stores in its own slot, warp sub - half folds it;
-      // named barrier of the SUB warps), warp 0 stages the result and all
-      // SUB store it, then release the region (mbarrier rfree) for the next
-      // unit's deposits.  The waits are bounded; on expiry a warp records
-      // the error and continues with an empty state.
-      const uint32_t kpar = static_cast<uint32_t>(k & 1);
-      auto sub_sync = [&] {
-        if constexpr (SUB > 1) named_barrier(1 + hh, SUB * 32);
-        else __syncwarp();
-      };
-      auto give_up = [&] {
-        record_error(p.err, kDeviceErrWaitTimeout);
-        sm.abort_flag = 1;
-        aborted = true;
-        l[0][0] = l[0][1] = 0.f;
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) o[mt][0][0] = o[mt][0][1] = o[mt][0][2] = o[mt][0][3] = 0.f;
-      };
-      if (late) {
-        if (k > 0 && !aborted && !mbar_wait(&sm.rfree[hh], kpar ^ 1u)) give_up();
-        put(0, sub);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.dfull[hh]);
-      } else {
-        if (!aborted && !mbar_wait(&sm.dfull[hh], kpar)) give_up();
-        if (!aborted) fold(0, sub);
-#pragma unroll
-        for (int half = SUB / 2; half >= 1; half >>= 1) {
-          if (sub >= half && sub < 2 * half) put(0, sub);
-          sub_sync();
-          if (sub < half) fold(0, sub + half);
-        }
-        finish_pair(sub == 0, sub_sync);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.rfree[hh]);
-      }
-    } else {
-      // ---- synchronous fold by halving over the R warps of the head
-      // (per column block): round 1, warp j >= R/2 stores in slot j - R/2
-      // and warp j - R/2 folds it; later rounds, warp j in [half, 2 half)
-      // stores in its own slot j (the one it read last round; no one else
-      // reads it) and warp j - half folds it.  Each head has its own named
-      // barrier; all warps of a head meet every one.
-      const int bar_id = 1 + hh, bar_n = R * 32;
+    }
+    // ---- the head's result, staged in its region as [q head][dim] fp32
+    // (8-float chunks XOR-swizzled by head: conflict-free fragment stores,
+    // 16-byte reads).  A pair this CTA met whole is stored as bf16 output
+    // with the gate (ops/qsa.py:250-275); a piece of a split pair as a
+    // normalised fp32 partial and its base-2 LSE in slot
+    // 2 * cta + (first pair met ? 0 : 1).
+    const bool whole = x.pieces == 1;
+    const int pslot = 2 * static_cast<int>(blockIdx.x) + (k == 0 ? 0 : 1);
+    named_barrier(bar_id, bar_n);
+    if (j == 0) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        named_barrier(bar_id, bar_n);  // region free: the previous contents were read
 #pragma unroll
-        for (int half = R / 2; half >= 1; half >>= 1) {
-          if (j >= half && j < 2 * half) {
-            __syncwarp();
-            put(nt, half == R / 2 ? j - half : j);
+        for (int hc = 0; hc < 2; ++hc) {
+          const int hl = 8 * nt + 2 * t4 + hc;
+          if (hl >= group) continue;
+          const float lv = l[nt][hc];
+          const float inv = lv > 0.f ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
+          float* srow = region + hl * D;
+          const int sw = (hl >> 1) & 3;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            srow[(((2 * mt) ^ sw) << 3) + g] = o[mt][nt][hc] * inv;
+            srow[(((2 * mt + 1) ^ sw) << 3) + g] = o[mt][nt][2 + hc] * inv;
           }
-          named_barrier(bar_id, bar_n);
-          if (j < half) fold(nt, half == R / 2 ? j : j + half);
+          if (!whole && g == 0)
+            p.part_lse[static_cast<int64_t>(pslot) * hqp + head0 + hl] =
+                lv > 0.f ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
         }
       }
-      named_barrier(bar_id, bar_n);
-      finish_pair(j == 0, [&] { named_barrier(bar_id, bar_n); });
+    }
+    named_barrier(bar_id, bar_n);
+    if (whole) {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int item = tr + i * R * 32;
+        if (item >= group * (D / 8)) continue;
+        const int hl = item / (D / 8), c = item % (D / 8);
+        const float4* src =
+            reinterpret_cast<const float4*>(region + hl * D + ((c ^ ((hl >> 1) & 3)) << 3));
+        store_out8(p, x.row, x.hg * hqp + head0 + hl, c * 8, src[0], src[1], gpre[i]);
+      }
+    } else {
+      float4* po = reinterpret_cast<float4*>(p.part_o +
+                                             (static_cast<int64_t>(pslot) * hqp + head0) * D);
+      for (int item = tr; item < group * (D / 4); item += R * 32) {
+        const int hl = item / (D / 4), c4 = item % (D / 4);
+        po[item] = *reinterpret_cast<const float4*>(
+            region + hl * D + (((c4 >> 1) ^ ((hl >> 1) & 3)) << 3) + (c4 & 1) * 4);
+      }
     }
   }
 }
@@ -810,10 +752,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.qfull[b], 1);
       mbar_init(&sm.qempty[b], kConsumerWarps);
-    }
-    for (int h = 0; h < HB; ++h) {  // one arrival per warp of a consumer group's share of h
-      mbar_init(&sm.dfull[h], kGroupWarps / HB);
-      mbar_init(&sm.rfree[h], kGroupWarps / HB);
     }
     sm.abort_flag = 0;
     fence_mbar_init();
