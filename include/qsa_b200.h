@@ -273,11 +273,12 @@ QSA_API int qsa_prepare(
 
 /*
  * Workspace bytes qsa_sparse_attention needs for these shapes on the current
- * device: fp32 partial outputs + LSE of the (row, KV-head group) pairs that
- * the work split cuts between two or more CTAs, combined by the merge pass.
- * At most 2 x SMs x (query heads of a pair, <= 32) x (head_dim + 1) x 4
- * bytes, whatever the row count (4.9 MB on a 148-SM B200), and 0 when no
- * pair is cut.  Deterministic in its arguments for a given device.
+ * device: fp32 per-warp partial outputs + LSE of the (row, KV-head group)
+ * pairs that the work split cuts between two or more CTAs, combined by the
+ * merge pass.  At most 2 x SMs x 8 x (query heads per KV head, <= 16) x
+ * (head_dim + 1) x 4 bytes, whatever the row count (19.6 MB on a 148-SM
+ * B200; 9.8 MB at 8 query heads per KV head), and 0 when no pair is cut.
+ * Deterministic in its arguments for a given device.
  */
 QSA_API size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
                                             int32_t num_kv_heads, int32_t head_dim,
@@ -333,14 +334,14 @@ QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_
  *   - Shapes are validated first (QSA_ERR_INVALID / QSA_ERR_UNSUPPORTED).
  *     The scratch need (qsa_sparse_attention_workspace_bytes) does not grow
  *     with the rows and fits QSA_STATIC_SCRATCH_BYTES on GPUs of up to 254
- *     SMs; a call needing more returns QSA_ERR_WORKSPACE.
+ *     SMs at any shape; a call needing more returns QSA_ERR_WORKSPACE.
  *   - Nothing in the scratch has to start at zero: each call writes every
  *     partial slot it reads (as an empty partial when a bounded wait gave up).
  *   - One scratch array serves all calls on a device: calls whose kernels
  *     overlap on the GPU (other streams or host threads) race on it; the
  *     caller must serialise them.
  */
-#define QSA_STATIC_SCRATCH_BYTES ((size_t)8 << 20)
+#define QSA_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
 QSA_API int qsa_sparse_attention_static_scratch(
     const void* q, int64_t q_row_stride, int64_t q_head_stride, int32_t rows,
     int32_t num_q_heads, int32_t head_dim, const void* k_cache, int64_t k_block_stride,

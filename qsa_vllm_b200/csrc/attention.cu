@@ -30,12 +30,12 @@
 //    group as N (no padding lanes at group 8), in two independent
 //    accumulator chains; P^T is transposed in registers (movmatrix) into the
 //    B operand of O^T = V^T.P^T.
-//  * At the end of a pair the softmax states of the warps that share a KV
-//    head are folded together in shared memory.  A pair met by one CTA only
-//    (the common case at prefill) is finished there: normalised, rounded to
-//    bf16, gated and stored.  A range boundary inside a pair splits it:
-//    each piece writes a normalised fp32 partial + LSE (the reference's
-//    split-K format) and a small merge kernel combines the at most
+//  * A pair met by one CTA only (the common case at prefill) is finished
+//    there: the softmax states of the warps that share a KV head are folded
+//    in shared memory, normalised, rounded to bf16, gated and stored.  A
+//    range boundary inside a pair splits it: each consumer warp writes its
+//    piece's normalised fp32 partial + LSE (the reference's split-K format)
+//    straight from registers, and a small merge kernel combines the at most
 //    sk_ctas - 1 split pairs.
 #include <algorithm>
 #include <cmath>
@@ -606,7 +606,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
     }
 
-    // ---- unit end: fold the softmax states of the R warps sharing a KV
+    // ---- unit end of a pair this CTA met whole: fold the softmax states of the R warps sharing a KV
     // head by halving.  Each head has its own shared-memory region (32 D / HB
     // floats: R / 2 exchange slots of (D / 16) float4 per lane, later its
     // GQA group's [head][dim] result) and its own named barrier, so heads do
@@ -633,6 +633,33 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 8);
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 16);
       }
+    if (x.pieces > 1) {
+      // ---- a piece of a split pair: this warp's normalised partial and its
+      // base-2 LSE (the reference's split-K format), written straight from
+      // registers with no fold and no barrier, in slot
+      // (2 * cta + (first pair met ? 0 : 1)) * R + rank of the warp.
+      const int slot =
+          (2 * static_cast<int>(blockIdx.x) + (k == 0 ? 0 : 1)) * R + cg * SUB + sub;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          const int hl = 8 * nt + 2 * t4 + hc;
+          if (hl >= group) continue;
+          const float lv = l[nt][hc];
+          const float inv = lv > 0.f ? 1.f / fmaxf(lv, 1.0e-20f) : 0.f;
+          const int64_t base = static_cast<int64_t>(slot) * hqp + head0 + hl;
+          float* po = p.part_o + base * D;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            po[mt * 16 + g] = o[mt][nt][hc] * inv;
+            po[mt * 16 + g + 8] = o[mt][nt][2 + hc] * inv;
+          }
+          if (g == 0) p.part_lse[base] = lv > 0.f ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
+        }
+      }
+      continue;
+    }
     float* region = sm.comb + hh * (32 * D / HB);
     float4* slots4 = reinterpret_cast<float4*>(region);
     const int bar_id = 1 + hh, bar_n = R * 32;
@@ -683,14 +710,10 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         }
       }
     }
-    // ---- the head's result, staged in its region as [q head][dim] fp32
-    // (8-float chunks XOR-swizzled by head: conflict-free fragment stores,
-    // 16-byte reads).  A pair this CTA met whole is stored as bf16 output
-    // with the gate (ops/qsa.py:250-275); a piece of a split pair as a
-    // normalised fp32 partial and its base-2 LSE in slot
-    // 2 * cta + (first pair met ? 0 : 1).
-    const bool whole = x.pieces == 1;
-    const int pslot = 2 * static_cast<int>(blockIdx.x) + (k == 0 ? 0 : 1);
+    // ---- the pair's result (this CTA met it whole), staged in the head's
+    // region as [q head][dim] fp32 (8-float chunks XOR-swizzled by head:
+    // conflict-free fragment stores, 16-byte reads), then stored as bf16
+    // output with the gate (ops/qsa.py:250-275).
     named_barrier(bar_id, bar_n);
     if (j == 0) {
 #pragma unroll
@@ -708,31 +731,18 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
             srow[(((2 * mt) ^ sw) << 3) + g] = o[mt][nt][hc] * inv;
             srow[(((2 * mt + 1) ^ sw) << 3) + g] = o[mt][nt][2 + hc] * inv;
           }
-          if (!whole && g == 0)
-            p.part_lse[static_cast<int64_t>(pslot) * hqp + head0 + hl] =
-                lv > 0.f ? m[nt][hc] + log2f(fmaxf(lv, 1.0e-20f)) : -INFINITY;
         }
       }
     }
     named_barrier(bar_id, bar_n);
-    if (whole) {
 #pragma unroll
-      for (int i = 0; i < kItems; ++i) {
-        const int item = tr + i * R * 32;
-        if (item >= group * (D / 8)) continue;
-        const int hl = item / (D / 8), c = item % (D / 8);
-        const float4* src =
-            reinterpret_cast<const float4*>(region + hl * D + ((c ^ ((hl >> 1) & 3)) << 3));
-        store_out8(p, x.row, x.hg * hqp + head0 + hl, c * 8, src[0], src[1], gpre[i]);
-      }
-    } else {
-      float4* po = reinterpret_cast<float4*>(p.part_o +
-                                             (static_cast<int64_t>(pslot) * hqp + head0) * D);
-      for (int item = tr; item < group * (D / 4); item += R * 32) {
-        const int hl = item / (D / 4), c4 = item % (D / 4);
-        po[item] = *reinterpret_cast<const float4*>(
-            region + hl * D + (((c4 >> 1) ^ ((hl >> 1) & 3)) << 3) + (c4 & 1) * 4);
-      }
+    for (int i = 0; i < kItems; ++i) {
+      const int item = tr + i * R * 32;
+      if (item >= group * (D / 8)) continue;
+      const int hl = item / (D / 8), c = item % (D / 8);
+      const float4* src =
+          reinterpret_cast<const float4*>(region + hl * D + ((c ^ ((hl >> 1) & 3)) << 3));
+      store_out8(p, x.row, x.hg * hqp + head0 + hl, c * 8, src[0], src[1], gpre[i]);
     }
   }
 }
@@ -767,25 +777,28 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnParams
 
 // Merge of the split pairs: the reference's split-K merge (ops/qsa.py:306-362)
 // over the pieces of each pair that a range boundary cuts.  Block column x
-// takes the pair that CTA b = split_cta[x]'s range ends in (b holds the pair's
+// takes the pair that CTA b = split.cta[x]'s range ends in (b holds the pair's
 // first tile and a later CTA its last), so each split pair has one block
-// column (grid.y blocks cover its heads).  The pieces are the partial slots
-// of CTAs o1..o2:
+// column (grid.y blocks cover its heads).  Each CTA o1..o2 meeting the pair
+// left R = 8 / heads_per_unit per-warp partials in its slot group:
 // 2*o1 + 1 (2*o1 when o1's range starts at the pair), then 2*c for the later
-// CTAs, for which it is the first pair met.  Weights 2^(lse - max lse); bf16
-// rounding and the optional sigmoid gate follow.  A block of 8 warps serves
-// 8 / W heads of the pair, W warps per head (from the plan's most pieces of
-// a pair, so that each warp loads one batch of 4 pieces in the common case);
-// a lane holds 4 dims.  The W states of a head are combined in shared memory.
+// CTAs, for which it is the first pair met; partial slot = group * R + warp.
+// Weights 2^(lse - max lse); bf16 rounding and the optional sigmoid gate
+// follow.  A block of 8 warps serves 8 / W heads of the pair, W warps per
+// head (from the plan's most partials of a split pair, so that each warp
+// loads one batch of 8 in the common case); a lane holds 4 dims.  The W
+// states of a head are combined in shared memory.
 constexpr int kMergeThreads = 256;
+constexpr int kMergeBatch = 8;  // partials a warp loads before using any
 template <int D, int W>
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p,
+                                                              const SplitList split) {
   constexpr int kHeads = 8 / W;  // heads per block
   __shared__ float4 st_o[W > 1 ? 8 : 1][32];
   __shared__ float st_m[8], st_d[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hl = warp / W, w = warp % W;
-  const int b = p.split_cta[blockIdx.x];
+  const int b = split.cta[blockIdx.x];
   const int64_t T = p.pair_tiles;
   const int64_t pair = (sk_begin(p, b + 1) - 1) / T;
   const int64_t first = pair * T;
@@ -810,25 +823,26 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
   }
   pdl_wait();
   pdl_trigger();
-  const int P = o2 - o1 + 1;
+  const int R = 8 / p.heads_per_unit;  // partials per piece
+  const int P = (o2 - o1 + 1) * R;     // partials of the pair
   const int e1 = sk_begin(p, o1) == first ? 0 : 1;
   float M = -INFINITY, den = 0.f;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int i0 = 4 * w; live && i0 < P; i0 += 4 * W) {
-    float lse[4];
-    float4 v[4];
+  for (int i0 = kMergeBatch * w; live && i0 < P; i0 += kMergeBatch * W) {
+    float lse[kMergeBatch];
+    float4 v[kMergeBatch];
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int i = i0 + jj;
-      const int64_t slot = i == 0 ? 2 * o1 + e1 : 2 * static_cast<int64_t>(o1 + i);
-      const int64_t base = i < P ? slot * hqp + h : 0;
+    for (int jj = 0; jj < kMergeBatch; ++jj) {
+      const int i = i0 + jj, piece = i / R;
+      const int64_t grp = piece == 0 ? 2 * o1 + e1 : 2 * static_cast<int64_t>(o1 + piece);
+      const int64_t base = i < P ? (grp * R + i % R) * hqp + h : 0;
       lse[jj] = i < P ? __ldg(p.part_lse + base) : -INFINITY;
       v[jj] = i < P ? __ldg(reinterpret_cast<const float4*>(p.part_o + base * D + d0))
                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float m_new = M;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) m_new = fmaxf(m_new, lse[jj]);
+    for (int jj = 0; jj < kMergeBatch; ++jj) m_new = fmaxf(m_new, lse[jj]);
     if (m_new == -INFINITY) continue;  // no valid piece yet
     const float r = M == -INFINITY ? 0.f : exp2f(M - m_new);
     den *= r;
@@ -836,7 +850,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
     for (int c = 0; c < 4; ++c) acc[c] *= r;
     M = m_new;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
+    for (int jj = 0; jj < kMergeBatch; ++jj) {
       const float wt = exp2f(lse[jj] - M);  // 0 for empty pieces
       den += wt;
       acc[0] += v[jj].x * wt;
@@ -889,26 +903,27 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
   op[1] = pack_bf16x2(o[2], o[3]);
 }
 
-// W warps per head: enough batches of 4 pieces for the plan's most pieces
-// of a split pair, at most 8.
+// W warps per head: enough batches of kMergeBatch partials for the plan's
+// most partials of a split pair (pieces x R), at most 8.
 template <int D>
-cudaError_t launch_merge(const AttnParams& p, cudaStream_t stream) {
-  const int batches = (p.merge_pieces + 3) / 4;
+cudaError_t launch_merge(const AttnParams& p, const SplitList& split, cudaStream_t stream) {
+  const int batches =
+      (p.merge_pieces * (8 / p.heads_per_unit) + kMergeBatch - 1) / kMergeBatch;
   const int W = batches <= 1 ? 1 : batches <= 2 ? 2 : batches <= 4 ? 4 : 8;
   const int hqp = p.heads_per_unit * (p.q_heads / p.kv_heads);
   const int heads_per_block = 8 / W;
-  const dim3 grid(p.n_split, (hqp + heads_per_block - 1) / heads_per_block);
+  const dim3 grid(split.n, (hqp + heads_per_block - 1) / heads_per_block);
   const dim3 block(kMergeThreads);
   switch (W) {
-    case 1: return count_launches(launch_kernel(merge_kernel<D, 1>, grid, block, 0, stream, 1, p));
-    case 2: return count_launches(launch_kernel(merge_kernel<D, 2>, grid, block, 0, stream, 1, p));
-    case 4: return count_launches(launch_kernel(merge_kernel<D, 4>, grid, block, 0, stream, 1, p));
-    default: return count_launches(launch_kernel(merge_kernel<D, 8>, grid, block, 0, stream, 1, p));
+    case 1: return count_launches(launch_kernel(merge_kernel<D, 1>, grid, block, 0, stream, 1, p, split));
+    case 2: return count_launches(launch_kernel(merge_kernel<D, 2>, grid, block, 0, stream, 1, p, split));
+    case 4: return count_launches(launch_kernel(merge_kernel<D, 4>, grid, block, 0, stream, 1, p, split));
+    default: return count_launches(launch_kernel(merge_kernel<D, 8>, grid, block, 0, stream, 1, p, split));
   }
 }
 
 template <int D, int NT, int HB>
-cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_dnh(const AttnParams& p, const SplitList& split, cudaStream_t stream) {
   static_assert(sizeof(Smem<D, NT, HB>) <= 227 * 1024, "shared memory above the opt-in limit");
   static_assert(HB * 8 * NT <= 32, "a pair's heads exceed the unit-end buffer");
   const size_t smem = sizeof(Smem<D, NT, HB>);
@@ -923,19 +938,19 @@ cudaError_t launch_dnh(const AttnParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   record_attention_event(1, stream);
   if (p.partials == 0) return cudaSuccess;  // no pair is split
-  return launch_merge<D>(p, stream);
+  return launch_merge<D>(p, split, stream);
 }
 
 template <int D, int NT>
-cudaError_t launch_dn(const AttnParams& p, int hb, cudaStream_t stream) {
+cudaError_t launch_dn(const AttnParams& p, const SplitList& split, int hb, cudaStream_t stream) {
   switch (hb) {
     case 4:
-      if constexpr (NT == 1) return launch_dnh<D, NT, 4>(p, stream);
+      if constexpr (NT == 1) return launch_dnh<D, NT, 4>(p, split, stream);
       break;
     case 2:
-      if constexpr (NT == 1) return launch_dnh<D, NT, 2>(p, stream);
+      if constexpr (NT == 1) return launch_dnh<D, NT, 2>(p, split, stream);
       break;
-    case 1: return launch_dnh<D, NT, 1>(p, stream);
+    case 1: return launch_dnh<D, NT, 1>(p, split, stream);
   }
   return cudaErrorInvalidValue;
 }
@@ -956,10 +971,11 @@ int attention_heads_per_unit(int q_heads, int kv_heads) {
 // Stream-K plan: U = pairs x pair_tiles units cut into one contiguous range
 // per CTA (one CTA per SM, or one per unit when there are fewer).  A pair is
 // split where a range boundary falls inside it; when any is, the workspace
-// holds two partial slots per CTA (the first and the last pair its range
-// meets), each [heads of a pair, dim] fp32 plus [heads of a pair] LSE, so
-// its size depends on the CTA count and the pair's heads, not on the rows.
-// The same integer arithmetic as the kernels.
+// holds two slot groups per CTA (the first and the last pair its range
+// meets), each one partial per consumer warp sharing a KV head (R = 8 / HB),
+// [heads of a pair, dim] fp32 plus [heads of a pair] LSE: its size depends
+// on the CTA count and the pair's heads, not on the rows.  The same integer
+// arithmetic as the kernels.
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
                         int use_decode_kernel) {
   (void)use_decode_kernel;
@@ -981,11 +997,11 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
     const int64_t o1 = owner(first), o2 = owner(first + T - 1);
     if (o1 == c && o2 > c) {
       plan.merge_pieces = std::max<int>(plan.merge_pieces, static_cast<int>(o2 - c + 1));
-      plan.split_cta[plan.n_split++] = static_cast<int16_t>(c);
+      plan.split.cta[plan.split.n++] = static_cast<int16_t>(c);
     }
   }
   if (plan.merge_pieces == 0) return plan;
-  plan.partials = 2;
+  plan.partials = 2 * (8 / hb);  // slot groups per CTA x partials per group
   const size_t hqp = static_cast<size_t>(hb) * (q_heads / kv_heads);
   const size_t slots = static_cast<size_t>(plan.partials) * plan.ctas;
   const size_t o_bytes = slots * hqp * dim * sizeof(float);
@@ -994,13 +1010,13 @@ AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_w
   return plan;
 }
 
-cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_attention(const AttnParams& p, const SplitList& split, cudaStream_t stream) {
   if (p.rows <= 0) return cudaSuccess;
   const int group = p.q_heads / p.kv_heads;
   const int nt = group <= 8 ? 1 : 2;
   const int hb = attention_heads_per_unit(p.q_heads, p.kv_heads);
-  if (p.dim == 128) return nt == 1 ? launch_dn<128, 1>(p, hb, stream) : launch_dn<128, 2>(p, hb, stream);
-  if (p.dim == 64) return nt == 1 ? launch_dn<64, 1>(p, hb, stream) : launch_dn<64, 2>(p, hb, stream);
+  if (p.dim == 128) return nt == 1 ? launch_dn<128, 1>(p, split, hb, stream) : launch_dn<128, 2>(p, split, hb, stream);
+  if (p.dim == 64) return nt == 1 ? launch_dn<64, 1>(p, split, hb, stream) : launch_dn<64, 2>(p, split, hb, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -726,14 +726,12 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.heads_per_unit = plan.heads_per_unit;
   p.partials = plan.partials;
   p.merge_pieces = plan.merge_pieces;
-  p.n_split = plan.n_split;
-  std::copy(plan.split_cta, plan.split_cta + plan.n_split, p.split_cta);
   if (plan.partials > 0) {
     p.part_o = static_cast<float*>(workspace);
     p.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.lse_offset);
   }
   p.err = device_error_word();
-  cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_attention(p, plan.split, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, who);
   return QSA_OK;
 }

@@ -142,29 +142,33 @@ struct AttnParams {
   int sk_ctas;          // CTAs of the main kernel
   int64_t sk_units;     // pairs * pair_tiles
   int heads_per_unit;   // KV heads per pair
-  int partials;         // partial slots per CTA: 2 when some pair is split, else 0
+  int partials;         // partial slots per CTA: 2 x (8 / heads_per_unit) when some pair is split, else 0
   int merge_pieces;     // most CTAs meeting one split pair
-  int n_split;          // split pairs: merge grid columns
-  int16_t split_cta[kMaxSplit];  // per split pair, the CTA holding its first tile
-  float* part_o;    // [partials * sk_ctas, heads of a pair, dim] fp32
-  float* part_lse;  // [partials * sk_ctas, heads of a pair] fp32
+  float* part_o;    // [sk_ctas, 2, 8 / heads_per_unit, heads of a pair, dim] fp32
+  float* part_lse;  // [sk_ctas, 2, 8 / heads_per_unit, heads of a pair] fp32
   int* err;
+};
+// The split pairs, each named by the CTA holding its first tile: the merge
+// kernel's grid columns (kept out of AttnParams, which every attention CTA
+// reads).
+struct SplitList {
+  int n;
+  int16_t cta[kMaxSplit];
 };
 struct AttnPlan {
   int pair_tiles;     // token tiles per (row, kv-head group) pair
   int ctas;           // main-kernel CTAs (contiguous unit ranges)
   int64_t units;      // pairs * pair_tiles
   int heads_per_unit; // KV heads per pair
-  int partials;       // partial slots per CTA (2 when some pair is split, else 0)
+  int partials;       // partial slots per CTA (2 x 8 / heads_per_unit when some pair is split, else 0)
   int merge_pieces;   // most CTAs meeting one split pair (0: none split)
-  int n_split;        // split pairs
-  int16_t split_cta[kMaxSplit];  // per split pair, the CTA holding its first tile
+  SplitList split;    // the split pairs
   size_t lse_offset;  // byte offset of the LSE slots in the workspace
   size_t workspace_bytes;
 };
 AttnPlan plan_attention(int rows, int q_heads, int kv_heads, int dim, int topk_width,
                         int use_decode_kernel);
-cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream);
+cudaError_t launch_attention(const AttnParams& p, const SplitList& split, cudaStream_t stream);
 
 // --------------------------------------------------------------- prepare
 struct PrepareParams {

@@ -70,18 +70,19 @@ def test_static_scratch_matches_caller_workspace_on_consecutive_calls():
 
 
 def test_static_scratch_need_does_not_grow_with_rows():
-    """The split-K scratch holds two partial slots per CTA, so the need is
-    bounded by the SM count, not the rows: every call fits the static array,
-    and a many-row call through it equals the caller-workspace path."""
+    """The split-K scratch holds two slot groups per CTA (one partial per
+    consumer warp), so the need is bounded by the SM count, not the rows:
+    every call fits the static array, and a many-row call through it equals
+    the caller-workspace path."""
     from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.ensure_device(dev)
     lib = _lib.load_library()
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    static_max = 8 << 20
+    static_max = 32 << 20
     for hq, hkv, d in ((32, 4, 128), (16, 2, 128), (16, 1, 128), (64, 4, 64), (8, 8, 128)):
-        bound = 256 + 2 * sms * 32 * (d + 1) * 4
+        bound = 256 + 2 * sms * 8 * (hq // hkv) * (d + 1) * 4
         for rows in (1, 64, 1024, 8192, 1 << 20):
             for width, decode in ((2051, 1), (1027, 0), (65539, 1)):
                 need = lib.qsa_sparse_attention_workspace_bytes(rows, hq, hkv, d, width, decode)
