@@ -139,8 +139,23 @@ def test_attention_workspace_query_is_deterministic():
     from qsa_vllm_b200.qsa import attention_workspace_bytes
     a = attention_workspace_bytes(64, 32, 4, 128, 2051, True)
     assert a == attention_workspace_bytes(64, 32, 4, 128, 2051, True)
-    # per-warp partials (O, LSE) of every split are always merged by a second kernel
+    # pairs cut by CTA range boundaries leave per-warp partials for the merge
     assert attention_workspace_bytes(8192, 16, 2, 128, 1027, False) > 0
+
+
+def test_attention_workspace_is_bounded_by_the_cta_count():
+    """Two slot groups per CTA of one partial per consumer warp (8) for the
+    GQA group, whatever the rows (148 SMs assumed without a device); 0 when
+    no pair is cut (one CTA per unit and every pair on one CTA)."""
+    from qsa_vllm_b200.qsa import attention_workspace_bytes
+    for hq, hkv, d in ((32, 4, 128), (16, 2, 128), (32, 2, 128), (16, 1, 64), (8, 8, 128)):
+        bound = 256 + 2 * 148 * 8 * (hq // hkv) * (d + 1) * 4
+        for rows in (1, 3, 64, 1000, 8192, 1 << 20):
+            for width in (1, 515, 2051, 65539):
+                need = attention_workspace_bytes(rows, hq, hkv, d, width, True)
+                assert 0 <= need <= bound, (hq, hkv, d, rows, width, need)
+    # 4 rows x 1 pair x 1 tile: 4 units on 4 CTAs, no pair cut
+    assert attention_workspace_bytes(4, 32, 4, 128, 16, True) == 0
 
 
 def test_operators_fail_loudly_without_a_gpu():
