@@ -606,15 +606,8 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
     }
 
-    // ---- unit end of a pair this CTA met whole: fold the softmax states of the R warps sharing a KV
-    // head by halving.  Each head has its own shared-memory region (32 D / HB
-    // floats: R / 2 exchange slots of (D / 16) float4 per lane, later its
-    // GQA group's [head][dim] result) and its own named barrier, so heads do
-    // not wait for each other.  Round 1: warp j >= R/2 stores its (O, m, l)
-    // in slot j - R/2 and warp j - R/2 folds it in; later rounds: warp j in
-    // [half, 2 half) stores in its own slot j, the one it read last round
-    // (no one else reads it), and warp j - half folds it in.  All warps of
-    // a head meet every barrier (aborted warps fold in an empty state).
+    // ---- unit end.  An aborted warp goes on with an empty state (l = 0,
+    // O = 0), so its partial or its share of the fold carries no weight.
     aborted = __any_sync(0xffffffffu, aborted);
     if (aborted) {
 #pragma unroll
@@ -660,6 +653,15 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
       continue;
     }
+    // ---- a pair this CTA met whole: fold the softmax states of the R warps
+    // sharing a KV head by halving.  Each head has its own shared-memory
+    // region (32 D / HB floats: R / 2 exchange slots of (D / 16) float4 per
+    // lane, later its GQA group's [head][dim] result) and its own named
+    // barrier, so heads do not wait for each other.  Round 1: warp j >= R/2
+    // stores its (O, m, l) in slot j - R/2 and warp j - R/2 folds it in;
+    // later rounds: warp j in [half, 2 half) stores in its own slot j, the
+    // one it read last round (no one else reads it), and warp j - half folds
+    // it in.  All warps of a head meet every barrier.
     float* region = sm.comb + hh * (32 * D / HB);
     float4* slots4 = reinterpret_cast<float4*>(region);
     const int bar_id = 1 + hh, bar_n = R * 32;
