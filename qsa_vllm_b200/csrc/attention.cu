@@ -313,6 +313,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     const int32_t* trow =
         p.block_table + static_cast<int64_t>(req_ok ? req : 0) * p.table_row_stride;
     const int64_t head0 = static_cast<int64_t>(x.hg) * HB;
+    const int64_t head_k = head0 * p.k_head_stride, head_v = head0 * p.v_head_stride;
     for (int t = x.t0; t < x.t1; ++t, ++it) {
       if (it % kProducers != pw) continue;  // another producer's tile
       const int s = it % kStages;
@@ -333,35 +334,37 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 
       uint8_t* stage = sm.stage[s];
       const int slot = own % kRing;
-      int64_t off_k[2], off_v[2];
-      int slot_id[2];  // physical slot (page * page_size + offset), -1 when masked
-      bool valid[2];
+      // Lane l handles tokens l and l + 32 of the tile; the second half
+      // exists only for one-head pairs (TT = 64).  Every instruction here
+      // is on the issue path that bounds L2-resident gathers.
+      constexpr int kHalves = TT > 32 ? 2 : 1;
+      int64_t off_k[kHalves];
+      int slot_id[kHalves];  // physical slot (page * page_size + offset), -1 when masked
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < kHalves; ++h) {
         const int j = lane + 32 * h;
         const int col = t * TT + j;
-        bool v = false;
-        int page = 0, off = 0;
+        int sl = -1, page = 0, off = 0;
         if (j < TT && col < x.n_cols) {
           const int tok = ring[slot][j];
-          int lp;
-          p.page_div.divmod(max(tok, 0), lp, off);
           if (p.physical) {
-            page = lp;
-            v = tok >= 0 && page < p.num_blocks;
+            if (tok >= 0 && static_cast<uint32_t>(tok) < p.num_slots) sl = tok;
           } else {
-            v = req_ok && tok >= 0 && lp < p.table_width;
-            page = v ? trow[lp] : -1;
-            v = v && page >= 0 && page < p.num_blocks;
+            int lp;
+            p.page_div.divmod(max(tok, 0), lp, off);
+            page = req_ok && tok >= 0 && lp < p.table_width ? trow[lp] : -1;
+            if (page >= 0 && page < p.num_blocks) sl = page * p.page_size + off;
           }
         }
-        valid[h] = v;
-        slot_id[h] = v ? page * p.page_size + off : -1;
-        off_k[h] = static_cast<int64_t>(page) * p.k_block_stride +
-                   static_cast<int64_t>(off) * p.k_token_stride + head0 * p.k_head_stride;
-        off_v[h] = static_cast<int64_t>(page) * p.v_block_stride +
-                   static_cast<int64_t>(off) * p.v_token_stride + head0 * p.v_head_stride;
-        if (!v && j < TT) {  // masked token: zeros, as the reference's masked loads
+        slot_id[h] = sl;
+        if (p.slot_contig) {  // block stride = page_size x token stride
+          off_k[h] = static_cast<int64_t>(max(sl, 0)) * p.k_token_stride + head_k;
+        } else {
+          if (p.physical) p.page_div.divmod(max(sl, 0), page, off);
+          off_k[h] = static_cast<int64_t>(page) * p.k_block_stride +
+                     static_cast<int64_t>(off) * p.k_token_stride + head_k;
+        }
+        if (sl < 0 && j < TT) {  // masked token: zeros, as the reference's masked loads
           uint4* z = reinterpret_cast<uint4*>(stage + S::tok_off(j));
 #pragma unroll 4
           for (int c = 0; c < kRow / 16; ++c) z[c] = make_uint4(0, 0, 0, 0);
@@ -370,16 +373,17 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       // Zero fills (generic proxy) are ordered before this stage's next bulk
       // copies (async proxy), issued after the full -> empty barrier chain;
       // without fills there is nothing to order.
-      if (__any_sync(0xffffffffu, (!valid[0] && lane < TT) || (!valid[1] && lane + 32 < TT)))
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      const unsigned lo = __ballot_sync(0xffffffffu, valid[0]);
-      const unsigned hi = __ballot_sync(0xffffffffu, valid[1]);
+      bool filled = slot_id[0] < 0 && lane < TT;
+      if constexpr (kHalves > 1) filled = filled || slot_id[1] < 0;
+      if (__any_sync(0xffffffffu, filled)) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const unsigned lo = __ballot_sync(0xffffffffu, slot_id[0] >= 0);
+      const unsigned hi = kHalves > 1 ? __ballot_sync(0xffffffffu, slot_id[kHalves - 1] >= 0) : 0u;
       // A 4-token block whose slots are consecutive in a slot-contiguous cache
       // is one run of 4*kRow bytes (4 selected tokens of one compressed block):
       // copy it whole.  cont bit j: token j+1 is the slot after token j.
-      unsigned cont[2];
+      unsigned cont[kHalves];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < kHalves; ++h) {
         const int nxt = __shfl_down_sync(0xffffffffu, slot_id[h], 1);
         cont[h] = __ballot_sync(0xffffffffu, slot_id[h] >= 0 && nxt == slot_id[h] + 1);
       }
@@ -389,8 +393,8 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       }
       __syncwarp();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!valid[h]) continue;
+      for (int h = 0; h < kHalves; ++h) {
+        if (slot_id[h] < 0) continue;
         const int j = lane + 32 * h;
         uint8_t* dst = stage + S::tok_off(j);
         const bool whole = p.kv_fused == 2 && p.slot_contig && p.kv_heads == HB &&
@@ -399,18 +403,22 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
           if ((lane & 3) == 0) bulk_g2s(dst, kbase + 2 * off_k[h], 4u * kRow, &sm.full[s]);
         } else if (p.kv_fused == 2) {  // all HB heads' K||V rows of the token contiguous
           bulk_g2s(dst, kbase + 2 * off_k[h], kRow, &sm.full[s]);
-        } else {
+        } else if (p.kv_fused == 1) {  // K||V adjacent per head
+#pragma unroll 1
+          for (int hh = 0; hh < HB; ++hh)
+            bulk_g2s(dst + hh * 4 * D, kbase + 2 * (off_k[h] + hh * p.k_head_stride), 4u * D,
+                     &sm.full[s]);
+        } else {  // K and V apart: V's own strides
+          int page, off;
+          p.page_div.divmod(slot_id[h], page, off);
+          const int64_t off_v = static_cast<int64_t>(page) * p.v_block_stride +
+                                static_cast<int64_t>(off) * p.v_token_stride + head_v;
 #pragma unroll 1
           for (int hh = 0; hh < HB; ++hh) {
-            if (p.kv_fused == 1) {
-              bulk_g2s(dst + hh * 4 * D, kbase + 2 * (off_k[h] + hh * p.k_head_stride), 4u * D,
-                       &sm.full[s]);
-            } else {
-              bulk_g2s(dst + hh * 4 * D, kbase + 2 * (off_k[h] + hh * p.k_head_stride), 2u * D,
-                       &sm.full[s]);
-              bulk_g2s(dst + hh * 4 * D + 2 * D, vbase + 2 * (off_v[h] + hh * p.v_head_stride),
-                       2u * D, &sm.full[s]);
-            }
+            bulk_g2s(dst + hh * 4 * D, kbase + 2 * (off_k[h] + hh * p.k_head_stride), 2u * D,
+                     &sm.full[s]);
+            bulk_g2s(dst + hh * 4 * D + 2 * D, vbase + 2 * (off_v + hh * p.v_head_stride), 2u * D,
+                     &sm.full[s]);
           }
         }
       }

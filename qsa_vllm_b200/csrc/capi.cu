@@ -687,6 +687,8 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
   p.v_head_stride = v_head_stride;
   p.num_blocks = num_blocks;
   p.page_size = page_size;
+  p.num_slots = static_cast<uint32_t>(
+      std::min<int64_t>(static_cast<int64_t>(num_blocks) * page_size, 0xffffffffll));
   p.page_div = FastDiv(static_cast<uint32_t>(page_size));
   p.kv_heads = num_kv_heads;
   p.indices = indices;

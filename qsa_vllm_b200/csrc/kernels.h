@@ -115,6 +115,7 @@ struct AttnParams {
   const void* v_cache;
   int64_t v_block_stride, v_token_stride, v_head_stride;
   int num_blocks, page_size, kv_heads;
+  uint32_t num_slots;  // num_blocks x page_size (clamped to 2^32 - 1)
   FastDiv page_div;  // division by page_size
   const int32_t* indices;
   int64_t indices_row_stride;
