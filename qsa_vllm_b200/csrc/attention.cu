@@ -278,6 +278,8 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   for (int i = 0; i < kLookahead; ++i) prefetch(i % kRing);
 
   int it = 0, k = 0, own = 0;
+  int next_own = pw;  // position of this producer's next own tile
+  constexpr int kOwnStages = kStages / kProducers;  // own tile n uses stage pw + kProducers * (n % kOwnStages)
 
   bool ok = true;
   for (; k < units && ok; ++k) {
@@ -315,18 +317,18 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     const int64_t head0 = static_cast<int64_t>(x.hg) * HB;
     const int64_t head_k = head0 * p.k_head_stride, head_v = head0 * p.v_head_stride;
     for (int t = x.t0; t < x.t1; ++t, ++it) {
-      if (it % kProducers != pw) continue;  // another producer's tile
-      const int s = it % kStages;
-      if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1)) {
+      if (it != next_own) continue;  // another producer's tile
+      next_own += kProducers;
+      const int s = pw + kProducers * (own % kOwnStages);  // = it % kStages
+      if (own >= kOwnStages && !mbar_wait(&sm.empty[s], ((own / kOwnStages) - 1) & 1)) {
         record_error(p.err, kDeviceErrWaitTimeout);
         sm.abort_flag = 1;
         ok = false;
         break;
       }
-      if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) {
-        ok = false;
-        break;
-      }
+      // read now, tested before the copies: the load's latency overlaps the
+      // offset arithmetic
+      const bool aborting = *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
       // token ids of this tile: this lane's own cp.async writes (same lane
       // mapping as the prefetch), complete once all but the newest
       // kLookahead-1 groups are.
@@ -386,6 +388,10 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       for (int h = 0; h < kHalves; ++h) {
         const int nxt = __shfl_down_sync(0xffffffffu, slot_id[h], 1);
         cont[h] = __ballot_sync(0xffffffffu, slot_id[h] >= 0 && nxt == slot_id[h] + 1);
+      }
+      if (aborting) {
+        ok = false;
+        break;
       }
       if (lane == 0) {
         sm.mask[s] = static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
