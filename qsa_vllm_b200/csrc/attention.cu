@@ -316,9 +316,11 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         p.block_table + static_cast<int64_t>(req_ok ? req : 0) * p.table_row_stride;
     const int64_t head0 = static_cast<int64_t>(x.hg) * HB;
     const int64_t head_k = head0 * p.k_head_stride, head_v = head0 * p.v_head_stride;
-    for (int t = x.t0; t < x.t1; ++t, ++it) {
-      if (it != next_own) continue;  // another producer's tile
-      next_own += kProducers;
+    // this producer's tiles of the unit: positions next_own, next_own + kProducers, ...
+    const int it0 = it;  // position of tile x.t0
+    for (int t = x.t0 + (next_own - it0); t < x.t1; t += kProducers) {
+      it = it0 + (t - x.t0);
+      next_own = it + kProducers;
       const int s = pw + kProducers * (own % kOwnStages);  // = it % kStages
       if (own >= kOwnStages && !mbar_wait(&sm.empty[s], ((own / kOwnStages) - 1) & 1)) {
         record_error(p.err, kDeviceErrWaitTimeout);
@@ -432,6 +434,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       prefetch((own + kLookahead) % kRing);
       ++own;
     }
+    if (ok) it = it0 + (x.t1 - x.t0);
   }
   // Drain: never leave while a copy into this CTA's shared memory may be in
   // flight.  Wait (bounded) for the last issued phase of every barrier.
