@@ -93,7 +93,8 @@ struct Smem {
 };
 
 struct Unit {
-  int row, hg, pieces, t0, t1, n_cols;  // pieces: CTAs whose ranges meet the pair
+  int row, hg, t0, t1, n_cols;
+  bool split;  // another CTA's range meets the pair too
 };
 
 // Stream-K split: CTA c owns units [U*c/C, U*(c+1)/C) of the U = pairs x
@@ -106,16 +107,23 @@ __device__ __forceinline__ int sk_owner(const AttnParams& p, int64_t x) {
   return static_cast<int>(((x + 1) * p.sk_ctas + p.sk_units - 1) / p.sk_units - 1);
 }
 
-// The k-th pair this CTA meets, its tile range inside the pair (clipped to
-// the row's valid tiles; may be empty) and its partial slot index.
+// The k-th pair this CTA meets (g0 = ua / pair_tiles: the first), its tile
+// range inside the pair (clipped to the row's valid tiles; may be empty) and
+// whether a range boundary splits it.  Called once per pair by every warp:
+// no 64-bit division except where a pair spans several KV-head groups.
 template <int TT>
-__device__ __forceinline__ Unit unit_of(const AttnParams& p, int groups, int64_t ua, int64_t ub,
-                                        int k) {
+__device__ __forceinline__ Unit unit_of(const AttnParams& p, int groups, int64_t g0, int64_t ua,
+                                        int64_t ub, int k) {
   Unit x;
   const int T = p.pair_tiles;
-  const int64_t g = ua / T + k;
-  x.hg = static_cast<int>(g % groups);
-  x.row = static_cast<int>(g / groups);
+  const int64_t g = g0 + k;
+  if (groups == 1) {
+    x.hg = 0;
+    x.row = static_cast<int>(g);
+  } else {
+    x.hg = static_cast<int>(g % groups);
+    x.row = static_cast<int>(g / groups);
+  }
   int n = p.topk_width;
   if (p.valid_counts != nullptr) n = min(max(p.valid_counts[x.row], 0), p.topk_width);
   x.n_cols = n;
@@ -125,7 +133,9 @@ __device__ __forceinline__ Unit unit_of(const AttnParams& p, int groups, int64_t
   const int t1 = static_cast<int>(min(ub, first + T) - first);
   x.t1 = min(t1, tiles);
   x.t0 = min(t0, x.t1);
-  x.pieces = sk_owner(p, first + T - 1) - sk_owner(p, first) + 1;
+  // The CTA ranges partition the units, and this one meets the pair: it is
+  // the only one to do so exactly when the pair lies inside its range.
+  x.split = first < ua || first + T > ub;
   return x;
 }
 
@@ -213,7 +223,7 @@ __device__ __forceinline__ void store_out8(const AttnParams& p, int row, int hea
 template <int TT>
 struct Cursor {
   int k, t, units, groups;
-  int64_t ua, ub;
+  int64_t g0, ua, ub;
   Unit x;
   bool live;
   __device__ void init(const AttnParams& p, int units_, int groups_, int64_t ua_, int64_t ub_) {
@@ -221,10 +231,11 @@ struct Cursor {
     groups = groups_;
     ua = ua_;
     ub = ub_;
+    g0 = ua / p.pair_tiles;
     k = 0;
     live = k < units;
     if (live) {
-      x = unit_of<TT>(p, groups, ua, ub, k);
+      x = unit_of<TT>(p, groups, g0, ua, ub, k);
       t = x.t0;
       skip(p);
     }
@@ -234,7 +245,7 @@ struct Cursor {
       ++k;
       live = k < units;
       if (live) {
-        x = unit_of<TT>(p, groups, ua, ub, k);
+        x = unit_of<TT>(p, groups, g0, ua, ub, k);
         t = x.t0;
       }
     }
@@ -248,6 +259,7 @@ struct Cursor {
 template <int D, int NT, int HB>
 __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups,
                          int64_t ua, int64_t ub) {
+  const int64_t g0 = ua / p.pair_tiles;  // first pair met
   using S = Smem<D, NT, HB>;
   constexpr int kRow = S::kRow;
   constexpr int TT = S::kTT;
@@ -283,7 +295,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 
   bool ok = true;
   for (; k < units && ok; ++k) {
-    const Unit x = unit_of<TT>(p, groups, ua, ub, k);
+    const Unit x = unit_of<TT>(p, groups, g0, ua, ub, k);
     // ---- the unit's query rows -> q[k & 1] (producer 0 only)
     const int qb = k & 1;
     if (pw == 0 && k >= 2 && !mbar_wait(&sm.qempty[qb], ((k >> 1) - 1) & 1)) {
@@ -452,6 +464,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 template <int D, int NT, int HB>
 __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, int groups,
                          int64_t ua, int64_t ub) {
+  const int64_t g0 = ua / p.pair_tiles;  // first pair met
   using S = Smem<D, NT, HB>;
   constexpr int TT = S::kTT;
   constexpr int SUB = kGroupWarps / HB;  // 16-token sub-tiles per stage per head
@@ -489,7 +502,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   constexpr int kItems = kOutItems<D, HB, NT>;
   const int head0 = hh * group;  // first query head of hh within the pair
   for (; k < units; ++k) {
-    const Unit x = unit_of<TT>(p, groups, ua, ub, k);
+    const Unit x = unit_of<TT>(p, groups, g0, ua, ub, k);
     const int qb = k & 1;
     // Rank j of this warp among the head's R warps for the unit-end fold:
     // the group that takes the unit's last tile (and so finishes last) ranks
@@ -504,7 +517,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
     uint4 gpre[kItems];
 #pragma unroll
     for (int i = 0; i < kItems; ++i) gpre[i] = make_uint4(0, 0, 0, 0);
-    if (p.gate != nullptr && x.pieces == 1) {
+    if (p.gate != nullptr && !x.split) {
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
         const int item = tr + i * R * 32;
@@ -643,7 +656,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 8);
         l[nt][hc] += __shfl_xor_sync(0xffffffffu, l[nt][hc], 16);
       }
-    if (x.pieces > 1) {
+    if (x.split) {
       // ---- a piece of a split pair: this warp's normalised partial and its
       // base-2 LSE (the reference's split-K format), written straight from
       // registers with no fold and no barrier, in slot
