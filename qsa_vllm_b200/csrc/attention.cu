@@ -233,26 +233,26 @@ struct Cursor {
     ub = ub_;
     g0 = ua / p.pair_tiles;
     k = 0;
+    t = 0;
     live = k < units;
     if (live) {
       x = unit_of<TT>(p, groups, g0, ua, ub, k);
       t = x.t0;
-      skip(p);
+      advance(p, 0);
     }
   }
-  __device__ void skip(const AttnParams& p) {
+  // Moves n positions on (tiles of later units count on from their t0).
+  __device__ void advance(const AttnParams& p, int n) {
+    t += n;
     while (live && t >= x.t1) {
+      const int over = t - x.t1;
       ++k;
       live = k < units;
       if (live) {
         x = unit_of<TT>(p, groups, g0, ua, ub, k);
-        t = x.t0;
+        t = x.t0 + over;
       }
     }
-  }
-  __device__ void next(const AttnParams& p) {
-    ++t;
-    skip(p);
   }
 };
 
@@ -273,7 +273,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
 
   Cursor<TT> ahead;  // this producer's own tiles: positions pw, pw + kProducers, ...
   ahead.init(p, units, groups, ua, ub);
-  for (int i = 0; i < pw; ++i) ahead.next(p);
+  ahead.advance(p, pw);
   auto prefetch = [&](int slot) {
     if (ahead.live) {
       const int32_t* idx_row = p.indices + static_cast<int64_t>(ahead.x.row) * p.indices_row_stride;
@@ -282,7 +282,7 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         const bool v = col < ahead.x.n_cols;
         cp_async4(&ring[slot][j], v ? idx_row + col : idx_row, v);
       }
-      for (int i = 0; i < kProducers; ++i) ahead.next(p);
+      ahead.advance(p, kProducers);
     }
     cp_async_commit();
   };
@@ -496,6 +496,9 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
   // reaches every named barrier, so no warp of the CTA is left waiting at one.
   bool aborted = false;
   int it = 0, k = 0;
+  // this group's next stage: cg + kGroups * gslot, barrier phase parity gphase
+  int gslot = 0;
+  uint32_t gphase = 0;
   const int hqp = HB * group;  // query heads of a pair
   // The R = 8 / HB warps sharing KV head hh.
   constexpr int R = kGroups * SUB;
@@ -560,12 +563,19 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       for (int mt = 0; mt < KS; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
     }
 
-    for (int t = x.t0; t < x.t1; ++t, ++it) {
-      if ((it % kGroups) != cg) continue;  // the other group's stage
-      const int s = it % kStages;
+    // this group's tiles of the unit: positions it0 + t - x.t0 = cg (mod kGroups)
+    const int it0 = it;
+    static_assert((kGroups & (kGroups - 1)) == 0, "kGroups is a power of two");
+    for (int t = x.t0 + ((cg - it0) & (kGroups - 1)); t < x.t1; t += kGroups) {
+      const int s = cg + kGroups * gslot;  // = position % kStages
+      const uint32_t parity = gphase;
+      if (++gslot == kStages / kGroups) {
+        gslot = 0;
+        gphase ^= 1;
+      }
       aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
       if (aborted) continue;
-      if (!mbar_wait(&sm.full[s], (it / kStages) & 1)) {
+      if (!mbar_wait(&sm.full[s], parity)) {
         record_error(p.err, kDeviceErrWaitTimeout);
         sm.abort_flag = 1;
         aborted = true;
@@ -635,6 +645,7 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         for (int nt = 0; nt < NT; ++nt) mma_bf16(o[mt][nt], va[mt], pb[nt][0], pb[nt][1]);
       }
     }
+    it = it0 + (x.t1 - x.t0);
 
     // ---- unit end.  An aborted warp goes on with an empty state (l = 0,
     // O = 0), so its partial or its share of the fold carries no weight.
