@@ -340,9 +340,6 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         ok = false;
         break;
       }
-      // read now, tested before the copies: the load's latency overlaps the
-      // offset arithmetic
-      const bool aborting = *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
       // token ids of this tile: this lane's own cp.async writes (same lane
       // mapping as the prefetch), complete once all but the newest
       // kLookahead-1 groups are.
@@ -402,10 +399,6 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       for (int h = 0; h < kHalves; ++h) {
         const int nxt = __shfl_down_sync(0xffffffffu, slot_id[h], 1);
         cont[h] = __ballot_sync(0xffffffffu, slot_id[h] >= 0 && nxt == slot_id[h] + 1);
-      }
-      if (aborting) {
-        ok = false;
-        break;
       }
       if (lane == 0) {
         sm.mask[s] = static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
@@ -573,7 +566,8 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         gslot = 0;
         gphase ^= 1;
       }
-      aborted = aborted || *reinterpret_cast<volatile int*>(&sm.abort_flag);
+      // Another role's abort shows here as a stage that never fills: the
+      // bounded wait below then ends this warp's work too.
       if (aborted) continue;
       if (!mbar_wait(&sm.full[s], parity)) {
         record_error(p.err, kDeviceErrWaitTimeout);
