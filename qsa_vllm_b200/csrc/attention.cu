@@ -386,11 +386,11 @@ __device__ void producer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
       // Zero fills (generic proxy) are ordered before this stage's next bulk
       // copies (async proxy), issued after the full -> empty barrier chain;
       // without fills there is nothing to order.
-      bool filled = slot_id[0] < 0 && lane < TT;
-      if constexpr (kHalves > 1) filled = filled || slot_id[1] < 0;
-      if (__any_sync(0xffffffffu, filled)) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       const unsigned lo = __ballot_sync(0xffffffffu, slot_id[0] >= 0);
       const unsigned hi = kHalves > 1 ? __ballot_sync(0xffffffffu, slot_id[kHalves - 1] >= 0) : 0u;
+      constexpr unsigned kLoLanes = TT >= 32 ? 0xffffffffu : (1u << (TT & 31)) - 1u;  // tokens 0..31
+      if ((~lo & kLoLanes) != 0u || (kHalves > 1 && ~hi != 0u))  // some token was zero-filled
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       // A 4-token block whose slots are consecutive in a slot-contiguous cache
       // is one run of 4*kRow bytes (4 selected tokens of one compressed block):
       // copy it whole.  cont bit j: token j+1 is the slot after token j.
@@ -575,9 +575,16 @@ __device__ void consumer(const AttnParams& p, Smem<D, NT, HB>& sm, int units, in
         aborted = true;
         continue;
       }
-      const uint64_t mask = sm.mask[s];
-      const bool v_lo = (mask >> row_tok(g)) & 1ull;
-      const bool v_hi = (mask >> row_tok(g + 8)) & 1ull;
+      bool v_lo, v_hi;
+      if constexpr (TT <= 32) {  // the stage's tokens fit the mask's low word
+        const uint32_t mask = static_cast<uint32_t>(sm.mask[s]);
+        v_lo = (mask >> row_tok(g)) & 1u;
+        v_hi = (mask >> row_tok(g + 8)) & 1u;
+      } else {
+        const uint64_t mask = sm.mask[s];
+        v_lo = (mask >> row_tok(g)) & 1ull;
+        v_hi = (mask >> row_tok(g + 8)) & 1ull;
+      }
       const uint32_t sbase = stage0 + static_cast<uint32_t>(s) * kStageBytes;
       // Pull this warp's K and V fragments into registers and hand the stage
       // back to the producer at once: the stage is held only for the
