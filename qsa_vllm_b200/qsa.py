@@ -22,6 +22,16 @@ def attention_workspace_bytes(rows: int, num_q_heads: int, num_kv_heads: int, he
         rows, num_q_heads, num_kv_heads, head_dim, topk_width, int(use_decode_kernel)))
 
 
+def aligned_head_rows(q: torch.Tensor) -> torch.Tensor:
+    """``q`` itself when every head row starts on a 16-byte boundary (the kernel
+    bulk-copies query rows), else a fresh contiguous copy.  ``.contiguous()``
+    would not do: it returns a contiguous view unchanged even when the view
+    starts at a misaligned element offset."""
+    if q.data_ptr() % 16 or q.stride(0) % 8 or q.stride(1) % 8:
+        return q.clone(memory_format=torch.contiguous_format)
+    return q
+
+
 def qsa_sparse_paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                                logical_indices: torch.Tensor, block_table: torch.Tensor,
                                token_to_req: torch.Tensor, out: torch.Tensor | None = None, *,
@@ -60,8 +70,7 @@ def qsa_sparse_paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: 
     gate = output_gate
     if gate is not None and gate.dtype != torch.bfloat16:
         raise TypeError("output_gate must be bfloat16")
-    if q.data_ptr() % 16 or q.stride(0) % 8 or q.stride(1) % 8:
-        q = q.contiguous()   # query rows are bulk-copied: 16-byte aligned head rows
+    q = aligned_head_rows(q)
     hq, d = q.shape[1], q.shape[2]
     hkv = k_cache.shape[2]
     width = logical_indices.shape[1]
@@ -92,4 +101,4 @@ def qsa_sparse_paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: 
     return out
 
 
-__all__ = ["qsa_sparse_paged_attention", "attention_workspace_bytes"]
+__all__ = ["qsa_sparse_paged_attention", "attention_workspace_bytes", "aligned_head_rows"]

@@ -405,6 +405,29 @@ def test_attention_strided_gate_and_output(dev, rows, hq, hkv, d, physical):
     assert torch.isnan(buf[:, :, :2].float()).all()   # nothing written outside the view
 
 
+def test_attention_misaligned_query_view(dev):
+    """A contiguous query view 2 bytes past a 16-byte boundary: the wrapper
+    copies it to aligned rows, and the output equals the aligned call's."""
+    from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
+    g = torch.Generator().manual_seed(11)
+    rows, hq, hkv, d, page, nblk = 6, 16, 2, 128, 16, 40
+    kv = torch.randn(nblk, page, hkv, 2 * d, generator=g).to(torch.bfloat16).to(dev)
+    q = (torch.randn(rows, hq, d, generator=g) * 0.3).to(torch.bfloat16).to(dev)
+    base = torch.empty(1 + rows * hq * d, dtype=torch.bfloat16, device=dev)
+    q_view = base[1:].view(rows, hq, d)
+    q_view.copy_(q)
+    assert q_view.is_contiguous() and q_view.data_ptr() % 16 == 2
+    idx = torch.randint(-1, nblk * page, (rows, 131), generator=g).to(torch.int32).to(dev)
+    table = torch.zeros(1, 1, dtype=torch.int32, device=dev)
+    t2r = torch.zeros(rows, dtype=torch.int32, device=dev)
+    outs = []
+    for qq in (q, q_view):
+        outs.append(qsa_sparse_paged_attention(qq, kv[..., :d], kv[..., d:], idx, table, t2r,
+                                               use_decode_kernel=True, indices_are_physical=True))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_attention_separate_kv_buffers(dev):
     """K and V in different allocations (two bulk copies per token)."""
     from qsa_vllm_b200.qsa import qsa_sparse_paged_attention

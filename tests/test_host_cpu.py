@@ -158,6 +158,26 @@ def test_attention_workspace_is_bounded_by_the_cta_count():
     assert attention_workspace_bytes(4, 32, 4, 128, 16, True) == 0
 
 
+def test_attention_query_rows_are_realigned_by_copy():
+    """A contiguous query view that starts 2 bytes past a 16-byte boundary is
+    copied (``.contiguous()`` would hand the same misaligned view back); an
+    aligned one, or one with aligned strides inside a wider row, is kept."""
+    from qsa_vllm_b200.qsa import aligned_head_rows
+    rows, hq, d = 3, 4, 128
+    base = torch.arange(1 + rows * hq * d, dtype=torch.float32).to(torch.bfloat16)
+    q = base[1:].view(rows, hq, d)
+    assert q.is_contiguous() and q.data_ptr() % 16 == 2
+    fixed = aligned_head_rows(q)
+    assert fixed.data_ptr() != q.data_ptr() and fixed.data_ptr() % 16 == 0
+    assert torch.equal(fixed, q)
+    aligned = torch.zeros(rows, hq, d, dtype=torch.bfloat16)
+    assert aligned_head_rows(aligned) is aligned
+    wide = torch.zeros(rows, hq + 2, d, dtype=torch.bfloat16)[:, 1:hq + 1]
+    assert aligned_head_rows(wide) is wide
+    odd_stride = torch.zeros(rows, hq * d + 4, dtype=torch.bfloat16)[:, :hq * d].view(rows, hq, d)
+    assert aligned_head_rows(odd_stride).stride(0) == hq * d
+
+
 def test_operators_fail_loudly_without_a_gpu():
     from qsa_vllm_b200 import _lib
     from qsa_vllm_b200.qsa import qsa_sparse_paged_attention
