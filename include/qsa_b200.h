@@ -278,6 +278,8 @@ QSA_API int qsa_prepare(
  * merge pass.  At most 2 x SMs x 8 x (query heads per KV head, <= 16) x
  * (head_dim + 1) x 4 bytes, whatever the row count (19.6 MB on a 148-SM
  * B200; 9.8 MB at 8 query heads per KV head), and 0 when no pair is cut.
+ * 0 as well for shapes qsa_sparse_attention rejects (no rows, non-positive
+ * head counts, query heads not a multiple of KV heads, negative width).
  * Deterministic in its arguments for a given device.
  */
 QSA_API size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,

@@ -302,7 +302,7 @@ int qsa_indexer_scores(const void* q, int64_t q_row_stride, int64_t q_head_strid
   if (head_dim != 64 && head_dim != 128)
     return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
   const bool pow2 = num_heads > 0 && num_heads <= 8 && (num_heads & (num_heads - 1)) == 0;
-  if (!(pow2 || (num_heads % 8 == 0 && num_heads <= 128)))
+  if (!(pow2 || (num_heads > 0 && num_heads % 8 == 0 && num_heads <= 128)))
     return fail(QSA_ERR_UNSUPPORTED, "%s: %d heads (supported: 1,2,4,8 or a multiple of 8)",
                 who, num_heads);
   if (page_size <= 0 || table_width < 0 || num_blocks < 0)
@@ -619,7 +619,9 @@ int qsa_prepare(const void* index_qk, int64_t index_row_stride, int32_t num_toke
 size_t qsa_sparse_attention_workspace_bytes(int32_t rows, int32_t num_q_heads,
                                             int32_t num_kv_heads, int32_t head_dim,
                                             int32_t topk_width, int32_t use_decode_kernel) {
-  if (rows <= 0 || num_kv_heads <= 0) return 0;
+  if (rows <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads ||
+      topk_width < 0)
+    return 0;  // no launch for these shapes (qsa_sparse_attention rejects them)
   return plan_attention(rows, num_q_heads, num_kv_heads, head_dim, topk_width, use_decode_kernel)
       .workspace_bytes;
 }
@@ -648,7 +650,7 @@ int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_head_str
     return fail(QSA_ERR_INVALID, "%s: logical indices need block_table and token_to_req", who);
   if (head_dim != 64 && head_dim != 128)
     return fail(QSA_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", who, head_dim);
-  if (num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads)
     return fail(QSA_ERR_INVALID, "%s: %d query heads not a multiple of %d kv heads", who,
                 num_q_heads, num_kv_heads);
   const int group = num_q_heads / num_kv_heads;

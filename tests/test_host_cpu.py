@@ -71,6 +71,20 @@ def test_argument_errors_are_reported_not_launched():
                                   2, 1024, 0, 8, None, 0, 0, 0, None, None, None, 0, 0, 0, 1024,
                                   0, 0, 1, 1, None, 0, None)
     assert st == 2 and b"group" in lib.qsa_last_error()
+    # non-positive head counts are refused before any launch (0 and -8 are
+    # multiples of 8 / of the KV heads, so they need their own check)
+    for heads in (0, -8):
+        st = lib.qsa_indexer_scores(1024, 64, 64, heads, 64, 1024, 0, 0, 1, 16, 1024, 0, 1, 1,
+                                    1024, None, None, 0, None, 0,
+                                    None, 1, 1, 0, 1, None, 0, 0, 1.0, 1024, 0, 8, None)
+        assert st == 2 and b"heads" in lib.qsa_last_error(), heads
+        st = lib.qsa_sparse_attention(1024, 0, 0, 1, heads, 128, 1024, 0, 0, 0, 1024, 0, 0, 0,
+                                      1, 16, 2, 1024, 0, 8, None, 0, 0, 0, None, None, None, 0,
+                                      0, 0, 1024, 0, 0, 1, 1, None, 0, None)
+        assert st == 1 and b"query heads" in lib.qsa_last_error(), heads
+        assert lib.qsa_sparse_attention_workspace_bytes(64, heads, 4, 128, 2051, 1) == 0
+    assert lib.qsa_sparse_attention_workspace_bytes(64, 30, 4, 128, 2051, 1) == 0
+    assert lib.qsa_sparse_attention_workspace_bytes(64, 32, 4, 128, -1, 1) == 0
     with pytest.raises(_lib.QSAError):
         _lib.check(1, "probe")
 
