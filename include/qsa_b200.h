@@ -107,6 +107,9 @@ enum {
  * lengths may be NULL: each row's length is then its visible block count
  * min((positions[r] + 1) // ratio, sequence_lengths[req] // ratio) (0 for an
  * unmapped row), as qsa_visible_blocks computes it.
+ * Limits (QSA_ERR_UNSUPPORTED beyond them): score_width up to 524288 columns
+ * (16-CTA clusters of 1024 threads x 32 keys), K up to 49152 blocks (one
+ * row's selection in 192 KB of shared memory); the same for qsa_topk.
  */
 QSA_API int qsa_topk_expand(const float* scores, int64_t score_row_stride, int32_t rows,
                     int32_t score_width, const int32_t* lengths, const int64_t* positions,

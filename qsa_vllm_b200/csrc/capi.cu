@@ -202,6 +202,9 @@ static int topk_common(TopkParams& p, void* stream, const char* who) {
   if (p.width > topk_max_width())
     return fail(QSA_ERR_UNSUPPORTED, "%s: score width %d exceeds %d", who, p.width,
                 topk_max_width());
+  if (p.topk > topk_max_blocks())
+    return fail(QSA_ERR_UNSUPPORTED, "%s: top-k of %d blocks exceeds %d", who, p.topk,
+                topk_max_blocks());
   p.vec4 = aligned(p.scores, 16) && (p.score_row_stride % 4 == 0);
   int cluster = 0;
   cudaError_t e = launch_topk(p, static_cast<cudaStream_t>(stream), &cluster);

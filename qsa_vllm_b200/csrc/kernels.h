@@ -40,6 +40,8 @@ struct TopkParams {
 cudaError_t launch_topk(const TopkParams& p, cudaStream_t stream, int* plan_cluster);
 // Largest score width the shared-memory-resident select supports.
 int topk_max_width();
+// Largest top-k (in blocks) one row's selection can hold in shared memory.
+int topk_max_blocks();
 
 // --------------------------------------------------------------- indexer
 struct IndexerParams {

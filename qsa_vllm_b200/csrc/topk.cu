@@ -564,6 +564,8 @@ cudaError_t launch_v(TopkParams p, int C, cudaStream_t stream) {
 
 int topk_max_width() { return kMaxCluster * kThreads * 32; }
 
+int topk_max_blocks() { return kMaxSelBytes / static_cast<int>(sizeof(int)); }
+
 cudaError_t launch_topk(const TopkParams& p0, cudaStream_t stream, int* plan_cluster) {
   TopkParams p = p0;
   if (p.rows <= 0) return cudaSuccess;

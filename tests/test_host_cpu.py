@@ -85,6 +85,10 @@ def test_argument_errors_are_reported_not_launched():
         assert lib.qsa_sparse_attention_workspace_bytes(64, heads, 4, 128, 2051, 1) == 0
     assert lib.qsa_sparse_attention_workspace_bytes(64, 30, 4, 128, 2051, 1) == 0
     assert lib.qsa_sparse_attention_workspace_bytes(64, 32, 4, 128, -1, 1) == 0
+    # a top-k beyond what one row's selection holds in shared memory (49152
+    # blocks) is refused with its own message, not a launch error
+    st = lib.qsa_topk(1024, 4096, 1, 4096, 1024, 1024, 49153, 49153, None)
+    assert st == 2 and b"top-k" in lib.qsa_last_error()
     with pytest.raises(_lib.QSAError):
         _lib.check(1, "probe")
 
