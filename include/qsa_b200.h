@@ -20,6 +20,12 @@
  *     detail for the calling host thread.  Invalid metadata VALUES (a -1 page,
  *     an out-of-range index) are not errors: they are masked exactly as the
  *     reference masks them.
+ *   - Per-device state (the device error word's address, kernel attributes,
+ *     the SM count) is looked up once per device and kept for the process:
+ *     the library expects each device's context to outlive its use, as torch
+ *     keeps the primary context; a process that resets a device
+ *     (cudaDeviceReset) must not call the library on it afterwards.
+ *     (The static-scratch entry point looks its array up on every call.)
  */
 #ifndef QSA_B200_H_
 #define QSA_B200_H_
