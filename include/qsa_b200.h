@@ -332,7 +332,13 @@ QSA_API int qsa_sparse_attention(const void* q, int64_t q_row_stride, int64_t q_
 
 /*
  * qsa_sparse_attention for callers that cannot allocate device memory.
- * No counterpart in the reference.  Same arguments and results as
+ * No counterpart in the reference.  Such callers are, for example, code that
+ * runs while a stream is captured in the global capture mode (a cudaMalloc
+ * there is refused and invalidates the capture), serving engines that hand
+ * all free device memory to their KV cache at start-up (a later cudaMalloc
+ * fails), and C callers without a caching allocator (a cudaMalloc / cudaFree
+ * per call synchronises the device and stalls the decode loop).  Same
+ * arguments and results as
  * qsa_sparse_attention without (workspace, workspace_bytes): the split-K
  * scratch is a file-scope device array of QSA_STATIC_SCRATCH_BYTES per device,
  * whose address is looked up (cudaGetSymbolAddress, no allocation) on each

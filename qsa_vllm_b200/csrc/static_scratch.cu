@@ -1,5 +1,8 @@
 // qsa_sparse_attention_static_scratch: paged sparse attention for callers that
-// cannot allocate device memory.  The split-K workspace (normalised partial
+// cannot allocate device memory -- code running under a global-mode stream
+// capture (cudaMalloc is refused there), engines whose KV cache took all free
+// memory at start-up, and C callers without a caching allocator (a cudaMalloc /
+// cudaFree per call would synchronise the device).  The split-K workspace (normalised partial
 // outputs + LSE) lives in a file-scope device array of QSA_STATIC_SCRATCH_BYTES
 // instead of a caller-provided buffer; nothing here allocates.
 //

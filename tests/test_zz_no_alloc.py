@@ -1,6 +1,10 @@
 """qsa_sparse_attention_static_scratch: the attention entry point that allocates
 nothing (split-K scratch in a static device array) against qsa_sparse_attention
-with a caller workspace.
+with a caller workspace.  It is meant for callers that cannot allocate device
+memory: code running under a global-mode stream capture (cudaMalloc is refused
+there), engines whose KV cache took all free memory at start-up, and C callers
+without a caching allocator (cudaMalloc / cudaFree per call would synchronise
+the device).
 
 Collected last (file name), and self-contained, so it runs the same alone in a
 fresh process and after the other GPU tests.
